@@ -1,0 +1,7 @@
+"""B200 (sm_100a) fused QKV projection, Q/K RMSNorm, NeoX RoPE and Ulysses
+exchange: a drop-in for joey-shao/flash_ulysses' ``FlashUlyssesContext``."""
+
+from .context import FlashUlyssesContext
+
+__version__ = "0.1.0"
+__all__ = ["FlashUlyssesContext"]

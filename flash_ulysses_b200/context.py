@@ -1,0 +1,212 @@
+"""Collective receive-buffer ownership and the public QKV interface.
+
+Drop-in for the reference's ``flash_ulysses.context.FlashUlyssesContext``
+(joey-shao/flash_ulysses ``flash_ulysses/context.py:9-174``): same constructor
+keywords, properties, ``ulysses_qkv_forward`` signature, output aliasing and
+``close()`` semantics.  Differences, all deliberate:
+
+* requires an sm_100 GPU (B200) instead of SM90 (context.py:59-60);
+* also admits ``sp_size == world_size == 1`` (a self-exchange on one GPU);
+  the reference requires ``sp_size >= 2`` (context.py:40);
+* receive buffers are plain ``cudaMalloc`` allocations shared through CUDA IPC
+  handles exchanged on ``control_group`` instead of ThunderKittens'
+  broker-based ``TKParallelTensor``; the exit barrier is fused into the kernel
+  and uses per-call epoch flags instead of a separate multicast barrier
+  launch;
+* a device-side wait that gives up (``timeout_s``) or a position outside the
+  RoPE cache sets a status word; the next call (or ``check()``) raises
+  ``RuntimeError`` instead of hanging.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import _C
+
+
+class FlashUlyssesContext:
+    """Construct, call and close collectively on one B200 node.
+
+    rank and world_size describe the participating physical GPUs on this node.
+    control_group must cover those same participants for lifecycle barriers and
+    the exchange of buffer handles.  Calls use the current CUDA stream.  Results
+    alias Q/K/V until the next call or close.  Before reuse, every physical rank
+    must finish consuming its previous output.
+    """
+
+    def __init__(
+        self,
+        *,
+        rank,
+        world_size,
+        max_local_tokens,
+        hidden_size=4096,
+        num_heads=32,
+        num_kv_heads=8,
+        head_dim=128,
+        sp_size=2,
+        control_group=None,
+        timeout_s=5.0,
+    ):
+        self.rank, self.world_size = rank, world_size
+        self.control_group = control_group
+        self.hidden_size = hidden_size
+        self.num_heads, self.num_kv_heads = num_heads, num_kv_heads
+        self.head_dim, self.sp_size = head_dim, sp_size
+        self.max_local_tokens = max_local_tokens
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self._op = None
+        self._status = None
+        self.Q = self.K = self.V = self.barrier = None
+
+        if not 1 <= sp_size <= self.world_size <= 8 or self.world_size % sp_size:
+            raise ValueError("SP must divide a single-node world of 1 to 8 GPUs")
+        if hidden_size <= 0 or hidden_size % 64 or head_dim != 128:
+            raise ValueError("Requires hidden_size > 0 divisible by 64 and head_dim=128")
+        if (
+            num_heads <= 0
+            or num_kv_heads <= 0
+            or num_heads % num_kv_heads
+            or num_heads % self.world_size
+            or num_kv_heads % self.world_size
+        ):
+            raise ValueError("Q heads must divide by KV heads; both must divide by world_size")
+        if max_local_tokens <= 0:
+            raise ValueError("max_local_tokens must be positive")
+        if torch.cuda.get_device_capability(self.device) != (10, 0):
+            raise ValueError("Requires SM100 (B200)")
+
+        group_start = rank // sp_size * sp_size
+        self.sp_rank = rank - group_start
+        peers = list(range(group_start, group_start + sp_size))
+        capacity = sp_size * max_local_tokens
+
+        def parallel(shape, dtype):
+            return _C.ParallelTensor(shape, dtype, rank, world_size, False,
+                                     group=control_group, peers=peers, device=self.device)
+
+        self.Q = parallel((capacity, self.output_q_heads * head_dim), torch.bfloat16)
+        self.K = parallel((capacity, self.output_kv_heads * head_dim), torch.bfloat16)
+        self.V = parallel((capacity, self.output_kv_heads * head_dim), torch.bfloat16)
+        # Per-rank synchronisation block: epoch flags written by SP peers and a
+        # CTA completion counter (layout in include/flash_ulysses_b200.h).
+        self.barrier = parallel((_C.FU_SYNC_WORDS,), torch.int32)
+        self.barrier.data_.zero_()
+        self._status = _C.StatusWord()
+
+        topo = _C.Topology()
+        topo.device = self.device.index
+        topo.sp_size = sp_size
+        topo.sp_rank = self.sp_rank
+        topo.q_heads = self.local_q_heads
+        topo.kv_heads = self.local_kv_heads
+        topo.hidden_size = hidden_size
+        topo.capacity_rows = capacity
+        for i, r in enumerate(peers):
+            topo.q_recv[i] = self.Q.peer_ptr(r)
+            topo.k_recv[i] = self.K.peer_ptr(r)
+            topo.v_recv[i] = self.V.peer_ptr(r)
+            topo.sync[i] = self.barrier.peer_ptr(r)
+        topo.status = self._status.device_ptr
+        topo.status_host = self._status.host_ptr
+        topo.timeout_ns = int(timeout_s * 1e9)
+        self._op = _C.QkvOp(topo)
+
+        torch.cuda.current_stream(self.device).synchronize()
+        if world_size > 1 or dist.is_initialized():
+            dist.barrier(group=control_group)
+
+    @property
+    def base_tp_size(self):
+        return self.world_size // self.sp_size
+
+    @property
+    def local_q_heads(self):
+        return self.num_heads // self.base_tp_size
+
+    @property
+    def local_kv_heads(self):
+        return self.num_kv_heads // self.base_tp_size
+
+    @property
+    def output_q_heads(self):
+        return self.num_heads // self.world_size
+
+    @property
+    def output_kv_heads(self):
+        return self.num_kv_heads // self.world_size
+
+    @property
+    def packed_width(self):
+        return (self.local_q_heads + 2 * self.local_kv_heads) * self.head_dim
+
+    @property
+    def epoch(self):
+        """Number of calls made so far (the value published to peers)."""
+        return self._op.epoch
+
+    @torch.no_grad()
+    def ulysses_qkv_forward(
+        self,
+        hidden_states,
+        qkv_weight,
+        positions,
+        q_norm_weight,
+        k_norm_weight,
+        rope_cache,
+        *,
+        q_epsilon=1e-6,
+        k_epsilon=1e-6,
+    ):
+        """Return BF16 (q, k, v), each with L * sp_size rows.
+
+        Inputs are contiguous CUDA tensors on the current/context device:
+        hidden_states BF16 [L, H], qkv_weight BF16 [H, packed_width],
+        positions int64 [L], norm weights FP32 [128], and a NeoX RoPE cache
+        FP32 [max_position, 128] containing [cos(64), sin(64)]. Positions must
+        index the cache. Epsilons must be positive. The caller crops padding.
+        """
+        local_tokens = hidden_states.size(0)
+        if not 0 < local_tokens <= self.max_local_tokens:
+            raise ValueError("Input length must be within [1, max_local_tokens]")
+        if self._status.value:
+            raise RuntimeError("an earlier call failed on the device: "
+                               + _C.decode_status(self._status.value))
+        _C.launch(hidden_states, qkv_weight, positions, q_norm_weight, k_norm_weight,
+                  rope_cache, self._op, q_epsilon=q_epsilon, k_epsilon=k_epsilon)
+        output_tokens = local_tokens * self.sp_size
+        return tuple(t.data()[:output_tokens] for t in (self.Q, self.K, self.V))
+
+    def check(self):
+        """Synchronise the device and raise if any call reported a device-side error."""
+        torch.cuda.synchronize(self.device)
+        if self._status.value:
+            raise RuntimeError("device-side error: " + _C.decode_status(self._status.value))
+
+    def clear_error(self):
+        """Reset the status word and the completion counter after a reported error
+        (call only when no launch of this context is in flight)."""
+        torch.cuda.synchronize(self.device)
+        self.barrier.data_[_C.FU_SYNC_COUNTER].zero_()
+        torch.cuda.synchronize(self.device)
+        self._status.clear()
+
+    def close(self):
+        """Collectively release peer mappings after all output consumers finish."""
+        torch.cuda.synchronize(self.device)
+        if self.world_size > 1 or dist.is_initialized():
+            dist.barrier(group=self.control_group)
+        with torch.cuda.device(self.device):
+            if self._op is not None:
+                self._op.destroy()
+                self._op = None
+            for name in ("Q", "K", "V", "barrier"):
+                t = getattr(self, name)
+                if t is not None:
+                    t.close()
+                setattr(self, name, None)
+            if self._status is not None:
+                self._status.free()
+                self._status = None

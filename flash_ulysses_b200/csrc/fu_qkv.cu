@@ -1,0 +1,686 @@
+// Fused QKV projection + Q/K RMSNorm + NeoX RoPE + Ulysses exchange for
+// B200 (sm_100a), one persistent launch per call.
+//
+// What it replaces: the reference's Hopper kernel and launcher
+// (joey-shao/flash_ulysses flash_ulysses/csrc/impl/flash_ulysses_kernel_hopper.cu:
+// kernel<N> 157-267, rmsnorm_and_rope 129-152, apply_neox_rope 86-125,
+// barrier_kernel 283-288, launch 305-353).  The reference's numerics differ
+// from its own PyTorch path (it keeps FP32 through the epilogue); this kernel
+// follows the PyTorch path's rounding points instead (tests/torch_base.py:52-64):
+// BF16 projection, FP32 norm, BF16, FP32 rotation, BF16.
+//
+// CTA layout (192 threads, one CTA per SM, persistent over tiles):
+//   warp 0      TMA producer: X tile [128 x 64] and W tile [64 x 256] per stage
+//   warp 1      TMEM owner + MMA issuer: tcgen05.mma M=128 N=256 K=16, FP32 in
+//               TMEM, two accumulator buffers of 256 columns
+//   warps 2..5  epilogue: one TMEM lane (= one token row) per thread; each
+//               thread holds a full 128-wide head row, so the RMSNorm sum and
+//               the NeoX partner (j, j+64) are thread-local; results are
+//               staged in swizzled shared memory and written by TMA bulk
+//               tensor stores directly into the destination rank's receive
+//               buffer (a peer GPU's memory mapped into this process).
+// A tile is 128 token rows x 2 heads (256 packed columns).  After its last
+// tile every CTA waits for its stores to complete and bumps a per-rank
+// counter; the last CTA of the rank publishes the call's epoch into every SP
+// member's flag word and waits (bounded) for theirs.
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "flash_ulysses_b200.h"
+#include "fu_internal.h"
+#include "fu_ptx.cuh"
+
+namespace fu {
+
+constexpr int BM = 128;                 // token rows per tile = TMEM lanes
+constexpr int BN = 256;                 // packed columns per tile = 2 heads
+constexpr int BK = 64;                  // reduction step: one 128-byte swizzle row
+constexpr int STAGES = 4;               // shared-memory pipeline depth
+constexpr int UMMA_K = 16;              // K of one tcgen05.mma kind::f16
+constexpr int NUM_THREADS = 192;
+constexpr int NUM_EPI_THREADS = 128;
+constexpr int A_STAGE_BYTES = BM * BK * 2;                    // 16 KiB
+constexpr int B_CHUNK_BYTES = BK * 64 * 2;                    // 8 KiB: 64 columns x BK rows
+constexpr int B_STAGE_BYTES = BK * BN * 2;                    // 32 KiB
+constexpr uint32_t STAGE_TX = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int BOX_BYTES = 32 * 128;                           // 32 rows x 64 BF16
+constexpr int STAGING_PER_WARP = 2 * BOX_BYTES;               // lo and hi halves of one head
+constexpr uint32_t TMEM_COLS = 512;
+
+constexpr int OFF_A = 0;
+constexpr int OFF_B = OFF_A + STAGES * A_STAGE_BYTES;
+constexpr int OFF_STG = OFF_B + STAGES * B_STAGE_BYTES;
+constexpr int OFF_BAR = OFF_STG + 4 * STAGING_PER_WARP;
+constexpr int NUM_BARS = 2 * STAGES + 2 + 2 + 1;
+constexpr int OFF_MISC = OFF_BAR + 128;
+constexpr int OFF_GAMMA = OFF_MISC + 64;
+constexpr int SMEM_BYTES = OFF_GAMMA + 2 * 128 * 4;
+constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;                 // room to align the base to 1 KiB
+static_assert(NUM_BARS * 8 <= 128, "barrier area");
+static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KiB per-CTA shared memory limit");
+
+// Where a wait gave up (second byte of the status word).
+enum : int { W_EMPTY = 1, W_FULL = 2, W_TEMPTY = 3, W_TFULL = 4, W_DRAIN = 5 };
+
+struct __align__(64) QkvParams {
+    CUtensorMap tm_x;                       // X [L, H]: box {64, 128}
+    CUtensorMap tm_w;                       // W [H, N]: box {64, 64}
+    CUtensorMap tm_out[3 * FU_MAX_SP];      // [component * FU_MAX_SP + dst]: {cols, L, S}
+    const int64_t* positions;
+    const float* q_gamma;
+    const float* k_gamma;
+    const float* rope;
+    __nv_bfloat16* gemm_out;
+    uint32_t* sync[FU_MAX_SP];
+    int32_t* status;
+    unsigned long long timeout_ns;
+    int32_t L, H, N, rope_rows;
+    int32_t heads, q_heads, kv_heads;
+    int32_t sp_size, sp_rank, q_per_gpu, kv_per_gpu;
+    int32_t num_n_blocks, num_tiles, k_blocks;
+    float q_eps, k_eps;
+    uint32_t epoch;
+    uint32_t wait_peers;
+};
+static_assert(sizeof(QkvParams) <= 4096, "kernel parameter block too large");
+
+__device__ __forceinline__ float bf16_round(float v) {
+    return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
+    __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&u);
+    return __bfloat1622float2(b);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&b);
+}
+
+// Bounded wait that ignores the abort flag: used only to drain in-flight
+// asynchronous work before the CTA exits.
+__device__ __forceinline__ bool drain_wait(uint32_t bar, uint32_t parity, uint64_t timeout_ns,
+                                           int32_t* status) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer_ns() - t0 > timeout_ns) {
+            report_status(status, FU_DEV_PIPELINE_TIMEOUT, W_DRAIN);
+            return false;
+        }
+    }
+    return true;
+}
+
+// ------------------------------------------------------------ roles
+__device__ void run_producer(const QkvParams& p, uint8_t* smem, uint32_t bar_full,
+                             uint32_t bar_empty, volatile int* abort_flag) {
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued_mask = 0;               // stages loaded at least once
+    uint32_t last_parity = 0;               // per-stage parity of the last load
+    const uint32_t a0 = smem_u32(smem + OFF_A);
+    const uint32_t b0 = smem_u32(smem + OFF_B);
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        const int m_blk = tile / p.num_n_blocks;
+        const int n_blk = tile % p.num_n_blocks;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+            if (!fu_wait_parity(bar_empty + 8 * stage, phase ^ 1u, abort_flag, p.timeout_ns,
+                                p.status, W_EMPTY)) {
+                ok = false;
+                break;
+            }
+            const uint32_t full = bar_full + 8 * stage;
+            mbar_arrive_expect_tx(full, STAGE_TX);
+            tma_load_2d(a0 + stage * A_STAGE_BYTES, &p.tm_x, full, kb * BK, m_blk * BM);
+            const uint32_t bdst = b0 + stage * B_STAGE_BYTES;
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c)
+                tma_load_2d(bdst + c * B_CHUNK_BYTES, &p.tm_w, full, n_blk * BN + c * 64, kb * BK);
+            issued_mask |= 1u << stage;
+            last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+            if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+    }
+    if (!ok) {
+        // Loads already issued must land before this CTA's shared memory is released.
+        for (int s = 0; s < STAGES; ++s)
+            if (issued_mask & (1u << s))
+                drain_wait(bar_full + 8 * s, (last_parity >> s) & 1u, p.timeout_ns, p.status);
+    }
+}
+
+__device__ void run_mma(const QkvParams& p, uint8_t* smem, uint32_t tmem_base, uint32_t bar_full,
+                        uint32_t bar_empty, uint32_t bar_tfull, uint32_t bar_tempty,
+                        uint32_t bar_mma_done, volatile int* abort_flag) {
+    constexpr uint32_t idesc = make_idesc_bf16_f32(BM, BN, /*a_mn_major=*/false,
+                                                   /*b_mn_major=*/true);
+    const uint32_t a0 = smem_u32(smem + OFF_A);
+    const uint32_t b0 = smem_u32(smem + OFF_B);
+    int stage = 0;
+    uint32_t phase = 0;
+    int local = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!fu_wait_parity(bar_tempty + 8 * acc, acc_phase ^ 1u, abort_flag, p.timeout_ns,
+                            p.status, W_TEMPTY)) {
+            ok = false;
+            break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+            if (!fu_wait_parity(bar_full + 8 * stage, phase, abort_flag, p.timeout_ns, p.status,
+                                W_FULL)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t a_base = a0 + stage * A_STAGE_BYTES;
+            const uint32_t b_base = b0 + stage * B_STAGE_BYTES;
+#pragma unroll
+            for (int k = 0; k < BK / UMMA_K; ++k) {
+                // A: K-major, 128B swizzle; K advances 32 bytes inside the swizzle row.
+                const uint64_t adesc = make_smem_desc_sw128(a_base + k * UMMA_K * 2, 16, 1024);
+                // B: MN-major, 128B swizzle; 64-column chunks are B_CHUNK_BYTES apart
+                // (leading offset), 8-row groups 1024 bytes apart (stride offset).
+                const uint64_t bdesc =
+                    make_smem_desc_sw128(b_base + k * UMMA_K * 128, B_CHUNK_BYTES, 1024);
+                tc_mma_bf16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
+            tc_commit(bar_empty + 8 * stage);      // frees the stage when these MMAs finish
+            if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+        if (ok) tc_commit(bar_tfull + 8 * acc);    // accumulator ready for the epilogue
+    }
+    // Every MMA this thread issued must finish before TMEM is released.
+    tc_commit(bar_mma_done);
+    drain_wait(bar_mma_done, 0, p.timeout_ns, p.status);
+}
+
+__device__ void run_epilogue(const QkvParams& p, uint8_t* smem, uint32_t tmem_base,
+                             uint32_t bar_tfull, uint32_t bar_tempty, const float* gam,
+                             volatile int* abort_flag) {
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int quarter = warp & 3;           // TMEM lanes this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    uint8_t* box_lo = smem + OFF_STG + (warp - 2) * STAGING_PER_WARP;
+    uint8_t* box_hi = box_lo + BOX_BYTES;
+    const uint32_t swz_row = lane * 128;
+    const int swz = lane & 7;
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+
+    int local = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        const int m_blk = tile / p.num_n_blocks;
+        const int n_blk = tile % p.num_n_blocks;
+        if (!fu_wait_parity(bar_tfull + 8 * acc, acc_phase, abort_flag, p.timeout_ns, p.status,
+                            W_TFULL))
+            break;
+        tc_fence_after();
+
+        const int m = m_blk * BM + row_in_tile;
+        const bool row_valid = m < p.L;
+        int64_t pos = 0;
+        if (row_valid) {
+            pos = __ldg(p.positions + m);
+            if (pos < 0 || pos >= p.rope_rows) {
+                report_status(p.status, FU_DEV_POSITION_RANGE, 0);
+                pos = 0;
+            }
+        }
+        const float* rope_row = p.rope + pos * 128;
+
+#pragma unroll 1
+        for (int hs = 0; hs < 2; ++hs) {
+            const int h = n_blk * 2 + hs;
+            if (h >= p.heads) break;        // odd head count: the last tile has one head
+
+            // TMEM -> registers, rounded to BF16 exactly as the BF16 projection output.
+            uint32_t packed[64];
+            float ss = 0.f;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t r[32];
+                tmem_ld_32cols(tmem_base + lane_addr + acc * BN + hs * 128 + c * 32, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const uint32_t u = pack_bf16x2(__uint_as_float(r[2 * i]),
+                                                   __uint_as_float(r[2 * i + 1]));
+                    packed[c * 16 + i] = u;
+                    const float2 f = unpack_bf16x2(u);
+                    ss = fmaf(f.x, f.x, ss);   // squares of BF16 values are exact in FP32
+                    ss = fmaf(f.y, f.y, ss);
+                }
+            }
+            if (hs == 1 || n_blk * 2 + 1 >= p.heads) {
+                // Both heads of this accumulator are in registers: hand TMEM back.
+                tc_fence_before();
+                mbar_arrive(bar_tempty + 8 * acc);
+            }
+
+            if (p.gemm_out != nullptr && row_valid) {
+                uint4* dst = reinterpret_cast<uint4*>(p.gemm_out + static_cast<int64_t>(m) * p.N +
+                                                      h * 128);
+#pragma unroll
+                for (int c = 0; c < 16; ++c)
+                    dst[c] = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
+                                        packed[4 * c + 3]);
+            }
+
+            int comp, head_id, per_gpu;
+            if (h < p.q_heads) {
+                comp = 0; head_id = h; per_gpu = p.q_per_gpu;
+            } else if (h < p.q_heads + p.kv_heads) {
+                comp = 1; head_id = h - p.q_heads; per_gpu = p.kv_per_gpu;
+            } else {
+                comp = 2; head_id = h - p.q_heads - p.kv_heads; per_gpu = p.kv_per_gpu;
+            }
+            const int dst = head_id / per_gpu;
+            const int dst_col = head_id % per_gpu;
+
+            // The staging boxes must have been read by the previous store.
+            if (lane == 0) bulk_wait_read_all();
+            __syncwarp();
+
+            if (comp < 2) {
+                const float eps = comp == 0 ? p.q_eps : p.k_eps;
+                const float* g = gam + comp * 128;
+                const float mean = ss * (1.0f / 128.0f);
+                const float scale = __frsqrt_rn(__fadd_rn(mean, eps));
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const float4 c0 = __ldg(reinterpret_cast<const float4*>(rope_row + 8 * c));
+                    const float4 c1 = __ldg(reinterpret_cast<const float4*>(rope_row + 8 * c + 4));
+                    const float4 s0 = __ldg(reinterpret_cast<const float4*>(rope_row + 64 + 8 * c));
+                    const float4 s1 =
+                        __ldg(reinterpret_cast<const float4*>(rope_row + 64 + 8 * c + 4));
+                    const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                    const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+                    uint32_t olo[4], ohi[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int j = 8 * c + 2 * i;
+                        const float2 lo = unpack_bf16x2(packed[4 * c + i]);
+                        const float2 hi = unpack_bf16x2(packed[32 + 4 * c + i]);
+                        // RMSNorm, * gamma, BF16 boundary (torch_base.py:56-61).
+                        const float nl0 = bf16_round(__fmul_rn(__fmul_rn(lo.x, scale), g[j]));
+                        const float nl1 = bf16_round(__fmul_rn(__fmul_rn(lo.y, scale), g[j + 1]));
+                        const float nh0 = bf16_round(__fmul_rn(__fmul_rn(hi.x, scale), g[j + 64]));
+                        const float nh1 = bf16_round(__fmul_rn(__fmul_rn(hi.y, scale), g[j + 65]));
+                        // NeoX rotation, separately rounded products (torch_base.py:62-63).
+                        const float r0 = __fsub_rn(__fmul_rn(nl0, cs[2 * i]), __fmul_rn(nh0, sn[2 * i]));
+                        const float r1 =
+                            __fsub_rn(__fmul_rn(nl1, cs[2 * i + 1]), __fmul_rn(nh1, sn[2 * i + 1]));
+                        const float t0 = __fadd_rn(__fmul_rn(nh0, cs[2 * i]), __fmul_rn(nl0, sn[2 * i]));
+                        const float t1 =
+                            __fadd_rn(__fmul_rn(nh1, cs[2 * i + 1]), __fmul_rn(nl1, sn[2 * i + 1]));
+                        olo[i] = pack_bf16x2(r0, r1);
+                        ohi[i] = pack_bf16x2(t0, t1);
+                    }
+                    const uint32_t off = swz_row + ((c ^ swz) << 4);
+                    *reinterpret_cast<uint4*>(box_lo + off) = make_uint4(olo[0], olo[1], olo[2], olo[3]);
+                    *reinterpret_cast<uint4*>(box_hi + off) = make_uint4(ohi[0], ohi[1], ohi[2], ohi[3]);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const uint32_t off = swz_row + ((c ^ swz) << 4);
+                    *reinterpret_cast<uint4*>(box_lo + off) = make_uint4(
+                        packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+                    *reinterpret_cast<uint4*>(box_hi + off) =
+                        make_uint4(packed[32 + 4 * c], packed[33 + 4 * c], packed[34 + 4 * c],
+                                   packed[35 + 4 * c]);
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                // Rows past L in this source's batch are clipped by the tensor map.
+                const CUtensorMap* tm = &p.tm_out[comp * FU_MAX_SP + dst];
+                const int row0 = m_blk * BM + quarter * 32;
+                tma_store_3d(tm, smem_u32(box_lo), dst_col * 128, row0, p.sp_rank);
+                tma_store_3d(tm, smem_u32(box_hi), dst_col * 128 + 64, row0, p.sp_rank);
+                bulk_commit_group();
+            }
+        }
+    }
+    if (lane == 0) {
+        bulk_wait_all();                    // peer writes performed
+        fence_proxy_async_global();
+    }
+    __syncwarp();
+}
+
+// ------------------------------------------------------------ kernel
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    const uint32_t bar_base = smem_u32(smem + OFF_BAR);
+    const uint32_t bar_full = bar_base;
+    const uint32_t bar_empty = bar_base + 8 * STAGES;
+    const uint32_t bar_tfull = bar_base + 16 * STAGES;
+    const uint32_t bar_tempty = bar_tfull + 16;
+    const uint32_t bar_mma_done = bar_tempty + 16;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
+    float* gam = reinterpret_cast<float*>(smem + OFF_GAMMA);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(bar_full + 8 * s, 1);
+            mbar_init(bar_empty + 8 * s, 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(bar_tfull + 8 * a, 1);
+            mbar_init(bar_tempty + 8 * a, NUM_EPI_THREADS);
+        }
+        mbar_init(bar_mma_done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&p.tm_x);
+        tma_prefetch_desc(&p.tm_w);
+    }
+    for (int i = threadIdx.x; i < 256; i += NUM_THREADS)
+        gam[i] = i < 128 ? p.q_gamma[i] : p.k_gamma[i - 128];
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == 0) {
+        if (lane == 0) run_producer(p, smem, bar_full, bar_empty, abort_flag);
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0)
+            run_mma(p, smem, tmem_base, bar_full, bar_empty, bar_tfull, bar_tempty, bar_mma_done,
+                    abort_flag);
+        __syncwarp();
+    } else {
+        run_epilogue(p, smem, tmem_base, bar_tfull, bar_tempty, gam, abort_flag);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+
+    // ---- exit barrier: the last CTA of this rank joins the SP group.
+    if (threadIdx.x == 64) {
+        const bool aborted = *abort_flag != 0;
+        uint32_t* my_sync = p.sync[p.sp_rank];
+        fence_acq_rel_sys();
+        const uint32_t old =
+            atom_add_acq_rel_gpu_u32(my_sync + FU_SYNC_COUNTER, aborted ? 0x10001u : 1u);
+        if ((old & 0xFFFFu) == gridDim.x - 1) {
+            const bool any_abort = aborted || (old >> 16) != 0;
+            *reinterpret_cast<volatile uint32_t*>(my_sync + FU_SYNC_COUNTER) = 0u;
+            if (!any_abort) {
+                fence_acq_rel_sys();
+                for (int d = 0; d < p.sp_size; ++d) st_release_sys_u32(p.sync[d] + p.sp_rank, p.epoch);
+                if (p.wait_peers) {
+                    const uint64_t t0 = globaltimer_ns();
+                    for (int s = 0; s < p.sp_size; ++s) {
+                        while (static_cast<int32_t>(ld_acquire_sys_u32(my_sync + s) - p.epoch) < 0) {
+                            if (globaltimer_ns() - t0 > p.timeout_ns) {
+                                report_status(p.status, FU_DEV_PEER_TIMEOUT, s);
+                                break;
+                            }
+                        }
+                    }
+                    fence_acq_rel_sys();
+                }
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------ host side
+// Signature of the driver's cuTensorMapEncodeTiled (cuda.h), fetched at run
+// time so the library needs no link-time dependency on libcuda.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void* ptr = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    });
+    return fn;
+}
+
+static int encode(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
+                  const cuuint64_t* strides_bytes, const cuuint32_t* box, const char* what) {
+    auto fn = encode_fn();
+    if (fn == nullptr) return set_error(FU_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint32_t elem_strides[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims,
+                    strides_bytes, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(FU_ERR_CUDA, "cuTensorMapEncodeTiled(%s) failed with %d", what,
+                         static_cast<int>(r));
+    return FU_OK;
+}
+
+}  // namespace fu
+
+struct fu_qkv_ctx {
+    fu_qkv_topology topo;
+    int sm_count = 0;
+    uint32_t epoch = 0;
+    int last_grid = 0;
+    // Tensor-map caches.
+    const void* x_ptr = nullptr;
+    int64_t x_rows = -1;
+    const void* w_ptr = nullptr;
+    int64_t out_rows = -1;
+    fu::QkvParams params;
+};
+
+using namespace fu;
+
+extern "C" int fu_qkv_create(const fu_qkv_topology* topo, fu_qkv_ctx** out) {
+    if (topo == nullptr || out == nullptr) return set_error(FU_ERR_INVALID, "null argument");
+    const int S = topo->sp_size;
+    if (S < 1 || S > FU_MAX_SP) return set_error(FU_ERR_INVALID, "sp_size %d not in [1, 8]", S);
+    if (topo->sp_rank < 0 || topo->sp_rank >= S)
+        return set_error(FU_ERR_INVALID, "sp_rank %d not in [0, %d)", topo->sp_rank, S);
+    if (topo->q_heads <= 0 || topo->kv_heads <= 0 || topo->q_heads % S || topo->kv_heads % S)
+        return set_error(FU_ERR_INVALID, "head counts (%d, %d) must be positive multiples of %d",
+                         topo->q_heads, topo->kv_heads, S);
+    if (topo->hidden_size <= 0 || topo->hidden_size % 64)
+        return set_error(FU_ERR_INVALID, "hidden_size %lld must be a positive multiple of 64",
+                         static_cast<long long>(topo->hidden_size));
+    if (topo->capacity_rows < S || topo->capacity_rows % S)
+        return set_error(FU_ERR_INVALID, "capacity_rows %lld must be a positive multiple of %d",
+                         static_cast<long long>(topo->capacity_rows), S);
+    for (int d = 0; d < S; ++d) {
+        if (!topo->q_recv[d] || !topo->k_recv[d] || !topo->v_recv[d] || !topo->sync[d])
+            return set_error(FU_ERR_INVALID, "missing buffer for SP member %d", d);
+        if ((reinterpret_cast<uintptr_t>(topo->q_recv[d]) | reinterpret_cast<uintptr_t>(topo->k_recv[d]) |
+             reinterpret_cast<uintptr_t>(topo->v_recv[d])) & 15)
+            return set_error(FU_ERR_INVALID, "receive buffers must be 16-byte aligned");
+    }
+    int dev_count = 0;
+    if (cudaGetDeviceCount(&dev_count) != cudaSuccess || topo->device < 0 ||
+        topo->device >= dev_count)
+        return set_error(FU_ERR_INVALID, "device %d is not available", topo->device);
+    int major = 0, minor = 0, sms = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, topo->device);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, topo->device);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, topo->device);
+    if (major != 10 || minor != 0)
+        return set_error(FU_ERR_UNSUPPORTED, "requires an sm_100 GPU (B200); device %d is sm_%d%d",
+                         topo->device, major, minor);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(topo->device);
+    cudaError_t e = cudaFuncSetAttribute(fused_qkv_exchange_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC);
+    cudaSetDevice(prev);
+    if (e != cudaSuccess)
+        return set_error(FU_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    auto* ctx = new fu_qkv_ctx();
+    ctx->topo = *topo;
+    if (ctx->topo.timeout_ns == 0) ctx->topo.timeout_ns = 5000000000ull;
+    ctx->sm_count = sms;
+    std::memset(&ctx->params, 0, sizeof(ctx->params));
+    *out = ctx;
+    return FU_OK;
+}
+
+extern "C" int fu_qkv_destroy(fu_qkv_ctx* ctx) {
+    delete ctx;
+    return FU_OK;
+}
+
+extern "C" uint32_t fu_qkv_epoch(const fu_qkv_ctx* ctx) { return ctx ? ctx->epoch : 0u; }
+extern "C" int fu_qkv_last_grid(const fu_qkv_ctx* ctx) { return ctx ? ctx->last_grid : 0; }
+
+extern "C" int fu_qkv_forward(fu_qkv_ctx* ctx, const void* x, const void* w,
+                              const int64_t* positions, const float* q_gamma,
+                              const float* k_gamma, const float* rope, int64_t local_tokens,
+                              int64_t rope_rows, double q_epsilon, double k_epsilon,
+                              uint32_t flags, void* stream, void* gemm_out) {
+    if (ctx == nullptr) return set_error(FU_ERR_INVALID, "null context");
+    const fu_qkv_topology& t = ctx->topo;
+    const int S = t.sp_size;
+    const int64_t L = local_tokens;
+    if (L < 1 || L * S > t.capacity_rows)
+        return set_error(FU_ERR_INVALID, "local_tokens %lld not in [1, %lld]",
+                         static_cast<long long>(L), static_cast<long long>(t.capacity_rows / S));
+    if (L > (int64_t(1) << 30)) return set_error(FU_ERR_INVALID, "local_tokens too large");
+    if (!x || !w || !positions || !q_gamma || !k_gamma || !rope)
+        return set_error(FU_ERR_INVALID, "null input pointer");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
+         reinterpret_cast<uintptr_t>(rope) | reinterpret_cast<uintptr_t>(gemm_out)) & 15)
+        return set_error(FU_ERR_INVALID, "x, w, rope and gemm_out must be 16-byte aligned");
+    if (rope_rows < 1) return set_error(FU_ERR_INVALID, "rope_rows must be positive");
+    if (t.status_host != nullptr && *reinterpret_cast<volatile int32_t*>(t.status_host) != 0)
+        return set_error(FU_ERR_DEVICE, "an earlier launch reported device status 0x%x",
+                         *t.status_host);
+
+    QkvParams& p = ctx->params;
+    const int64_t H = t.hidden_size;
+    const int heads = t.q_heads + 2 * t.kv_heads;
+    const int64_t N = static_cast<int64_t>(heads) * FU_HEAD_DIM;
+    int rc;
+    if (x != ctx->x_ptr || L != ctx->x_rows) {
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(L)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(H * 2)};
+        const cuuint32_t box[2] = {BK, BM};
+        if ((rc = encode(&p.tm_x, x, 2, dims, strides, box, "hidden_states")) != FU_OK) return rc;
+        ctx->x_ptr = x;
+        ctx->x_rows = L;
+    }
+    if (w != ctx->w_ptr) {
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(H)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(N * 2)};
+        const cuuint32_t box[2] = {64, BK};
+        if ((rc = encode(&p.tm_w, w, 2, dims, strides, box, "qkv_weight")) != FU_OK) return rc;
+        ctx->w_ptr = w;
+    }
+    if (L != ctx->out_rows) {
+        for (int comp = 0; comp < 3; ++comp) {
+            const int per_gpu = (comp == 0 ? t.q_heads : t.kv_heads) / S;
+            const int64_t cols = static_cast<int64_t>(per_gpu) * FU_HEAD_DIM;
+            for (int d = 0; d < S; ++d) {
+                void* base = comp == 0 ? t.q_recv[d] : (comp == 1 ? t.k_recv[d] : t.v_recv[d]);
+                // Destination d's buffer seen as [S sources][L rows][cols]: a tail tile
+                // is clipped at this source's L rows instead of spilling into the next.
+                const cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols),
+                                            static_cast<cuuint64_t>(L),
+                                            static_cast<cuuint64_t>(S)};
+                const cuuint64_t strides[2] = {static_cast<cuuint64_t>(cols * 2),
+                                               static_cast<cuuint64_t>(L * cols * 2)};
+                const cuuint32_t box[3] = {64, 32, 1};
+                if ((rc = encode(&p.tm_out[comp * FU_MAX_SP + d], base, 3, dims, strides, box,
+                                 "receive buffer")) != FU_OK)
+                    return rc;
+            }
+        }
+        ctx->out_rows = L;
+    }
+
+    p.positions = positions;
+    p.q_gamma = q_gamma;
+    p.k_gamma = k_gamma;
+    p.rope = rope;
+    p.gemm_out = static_cast<__nv_bfloat16*>(gemm_out);
+    for (int d = 0; d < FU_MAX_SP; ++d) p.sync[d] = d < S ? t.sync[d] : nullptr;
+    p.status = t.status;
+    p.timeout_ns = t.timeout_ns;
+    p.L = static_cast<int32_t>(L);
+    p.H = static_cast<int32_t>(H);
+    p.N = static_cast<int32_t>(N);
+    p.rope_rows = rope_rows > INT32_MAX ? INT32_MAX : static_cast<int32_t>(rope_rows);
+    p.heads = heads;
+    p.q_heads = t.q_heads;
+    p.kv_heads = t.kv_heads;
+    p.sp_size = S;
+    p.sp_rank = t.sp_rank;
+    p.q_per_gpu = t.q_heads / S;
+    p.kv_per_gpu = t.kv_heads / S;
+    p.num_n_blocks = (heads + 1) / 2;
+    const int64_t m_blocks = (L + BM - 1) / BM;
+    const int64_t tiles = m_blocks * p.num_n_blocks;
+    if (tiles > INT32_MAX) return set_error(FU_ERR_INVALID, "too many tiles");
+    p.num_tiles = static_cast<int32_t>(tiles);
+    p.k_blocks = static_cast<int32_t>(H / BK);
+    p.q_eps = static_cast<float>(q_epsilon);
+    p.k_eps = static_cast<float>(k_epsilon);
+    p.epoch = ++ctx->epoch;
+    if (p.epoch == 0) p.epoch = ++ctx->epoch;   // 0 is the flags' initial value
+    p.wait_peers = (flags & FU_FWD_NO_PEER_WAIT) ? 0u : 1u;
+
+    const int grid = static_cast<int>(tiles < ctx->sm_count ? tiles : ctx->sm_count);
+    ctx->last_grid = grid;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != t.device) cudaSetDevice(t.device);
+    fused_qkv_exchange_kernel<<<grid, NUM_THREADS, SMEM_ALLOC,
+                                static_cast<cudaStream_t>(stream)>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (prev != t.device) cudaSetDevice(prev);
+    if (e != cudaSuccess) return set_error(FU_ERR_CUDA, "launch failed: %s", cudaGetErrorString(e));
+    return FU_OK;
+}

@@ -1,0 +1,162 @@
+/*
+ * flash_ulysses_b200 -- C ABI of the fused Ulysses QKV operator for B200
+ * (sm_100a).
+ *
+ * The operator computes, for one rank of a single-node world of P GPUs split
+ * into SP groups of S consecutive ranks (base tensor parallelism T = P / S):
+ *
+ *   Y = X[L, H] @ W[H, N]                      BF16 in, FP32 accumulate, BF16 out
+ *   Q, K heads: RMSNorm (FP32) * gamma -> BF16 -> NeoX RoPE (FP32) -> BF16
+ *   V heads:    BF16 projection as is
+ *   Ulysses all-to-all: local packed head h of component c goes to SP member
+ *   h / (heads_c / S), head column h % (heads_c / S), rows [sp_rank * L, +L)
+ *
+ * and stores every output tile directly into the destination rank's receive
+ * buffer (its memory mapped into this process), then joins the SP group on
+ * per-call epoch flags.  Everything happens in one kernel launch on the
+ * caller's stream.
+ *
+ * All functions return 0 on success and a nonzero FU_ERR_* code otherwise;
+ * fu_last_error() describes the most recent failure on the calling thread.
+ * No function takes or returns framework (torch) types: plain pointers,
+ * sizes and CUDA stream handles only.
+ */
+#ifndef FLASH_ULYSSES_B200_H_
+#define FLASH_ULYSSES_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FU_API __attribute__((visibility("default")))
+#else
+#define FU_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FU_MAX_SP 8          /* largest SP group: one 8-GPU node */
+#define FU_HEAD_DIM 128      /* head dimension, as in the reference */
+#define FU_IPC_HANDLE_BYTES 64
+/* Per-rank synchronisation block (uint32 words), shared with the SP group:
+ *   [0, FU_MAX_SP)            exit flags: word p holds the last epoch SP member
+ *                             p finished writing into this rank
+ *   [FU_SYNC_COUNTER]         CTA completion counter (local use only)
+ */
+#define FU_SYNC_WORDS 64
+#define FU_SYNC_COUNTER 32
+
+enum fu_error {
+    FU_OK = 0,
+    FU_ERR_INVALID = 1,      /* bad argument (shape, pointer, topology) */
+    FU_ERR_CUDA = 2,         /* a CUDA runtime/driver call failed */
+    FU_ERR_UNSUPPORTED = 3,  /* device is not sm_100 or lacks a feature */
+    FU_ERR_DEVICE = 4        /* a previous launch reported a device-side error */
+};
+
+/* Device-side status codes (low byte of the status word; the next byte says
+ * which wait gave up). */
+enum fu_device_status {
+    FU_STATUS_OK = 0,
+    FU_STATUS_PIPELINE_TIMEOUT = 1,
+    FU_STATUS_PEER_TIMEOUT = 2,
+    FU_STATUS_POSITION_RANGE = 3
+};
+
+/* Flags for fu_qkv_forward. */
+#define FU_FWD_NO_PEER_WAIT 1u  /* signal peers but do not wait for them */
+
+FU_API const char* fu_last_error(void);
+FU_API int fu_version(void);
+
+/* ------------------------------------------------------------------------
+ * Receive buffers shared by the ranks of one node.  Replaces the symmetric
+ * allocation of ThunderKittens' TKParallelTensor (reference
+ * flash_ulysses/context.py:63-90, csrc/bindings.cu:16): every rank allocates
+ * its own buffer, exports a 64-byte handle, and opens every peer's handle.
+ * The handles are exchanged by the caller (e.g. torch.distributed on the
+ * control group), so no fixed-name broker is involved.
+ * ------------------------------------------------------------------------ */
+FU_API int fu_buffer_alloc(int device, size_t bytes, void** ptr);
+FU_API int fu_buffer_free(int device, void* ptr);
+FU_API int fu_buffer_export(int device, void* ptr, unsigned char handle[FU_IPC_HANDLE_BYTES]);
+FU_API int fu_buffer_import(int device, const unsigned char handle[FU_IPC_HANDLE_BYTES],
+                     void** peer_ptr);
+FU_API int fu_buffer_close(int device, void* peer_ptr);
+
+/* Host-mapped status word the kernel writes on a device-side error.  The
+ * host reads *host_ptr without synchronising. */
+FU_API int fu_status_alloc(int32_t** host_ptr, int32_t** device_ptr);
+FU_API int fu_status_free(int32_t* host_ptr);
+
+/* ------------------------------------------------------------------------
+ * The fused operator.
+ * ------------------------------------------------------------------------ */
+typedef struct fu_qkv_ctx fu_qkv_ctx;
+
+typedef struct fu_qkv_topology {
+    int32_t device;          /* CUDA device ordinal of this rank */
+    int32_t sp_size;         /* S: 1..FU_MAX_SP */
+    int32_t sp_rank;         /* this rank's index in its SP group */
+    int32_t q_heads;         /* local (post base-TP) query heads, divisible by S */
+    int32_t kv_heads;        /* local key/value heads, divisible by S */
+    int32_t reserved0;
+    int64_t hidden_size;     /* H, a positive multiple of 64 */
+    int64_t capacity_rows;   /* rows of every receive buffer: S * max_local_tokens */
+    /* Receive buffers of SP member p as mapped in this process (p == sp_rank
+     * is this rank's own).  Row-major BF16 [capacity_rows, heads_c/S * 128]. */
+    void* q_recv[FU_MAX_SP];
+    void* k_recv[FU_MAX_SP];
+    void* v_recv[FU_MAX_SP];
+    /* Synchronisation block (FU_SYNC_WORDS uint32, zero-initialised) of SP
+     * member p as mapped in this process. */
+    uint32_t* sync[FU_MAX_SP];
+    int32_t* status;         /* device pointer of a status word, may be NULL */
+    int32_t* status_host;    /* host view of the same word (fu_status_alloc), may be NULL;
+                                fu_qkv_forward refuses to launch while it is nonzero */
+    uint64_t timeout_ns;     /* bound on every device-side wait; 0 = 5 s */
+} fu_qkv_topology;
+
+/* Create the per-rank operator state (tensor-map caches, epoch counter).
+ * Replaces the descriptor set-up of the reference launcher
+ * (flash_ulysses_kernel_hopper.cu:305-347). */
+FU_API int fu_qkv_create(const fu_qkv_topology* topo, fu_qkv_ctx** out);
+FU_API int fu_qkv_destroy(fu_qkv_ctx* ctx);
+
+/* One fused call: projection + Q/K RMSNorm + NeoX RoPE + Ulysses exchange +
+ * exit barrier, as a single launch on `stream` (a cudaStream_t).
+ * Replaces flash_ulysses::launch (reference
+ * flash_ulysses/csrc/impl/flash_ulysses_kernel_hopper.cu:305-353, bound at
+ * csrc/bindings.cu:17 and called from context.py:144-160).
+ *
+ *   x          BF16 [local_tokens, H], row-major, 16-byte aligned
+ *   w          BF16 [H, (q_heads + 2 kv_heads) * 128], row-major, packed Q|K|V
+ *   positions  int64 [local_tokens], indices into rope
+ *   q_gamma, k_gamma  FP32 [128]
+ *   rope       FP32 [rope_rows, 128] = cos(64) | sin(64)
+ *   gemm_out   NULL, or BF16 [local_tokens, N]: test instrumentation that
+ *              also receives the BF16-rounded projection
+ *
+ * 1 <= local_tokens <= capacity_rows / S.  Every rank of the SP group must
+ * make the same sequence of calls; all ranks must have finished consuming
+ * the previous call's outputs before any rank calls again (reference
+ * README.md:67-70).  Returns FU_ERR_DEVICE without launching if an earlier
+ * launch left a nonzero status word. */
+FU_API int fu_qkv_forward(fu_qkv_ctx* ctx, const void* x, const void* w, const int64_t* positions,
+                   const float* q_gamma, const float* k_gamma, const float* rope,
+                   int64_t local_tokens, int64_t rope_rows, double q_epsilon,
+                   double k_epsilon, uint32_t flags, void* stream, void* gemm_out);
+
+/* Epoch of the most recent call (the value written into peers' flags). */
+FU_API uint32_t fu_qkv_epoch(const fu_qkv_ctx* ctx);
+
+/* Number of CTAs the most recent call launched (persistent grid). */
+FU_API int fu_qkv_last_grid(const fu_qkv_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASH_ULYSSES_B200_H_ */
