@@ -1,0 +1,439 @@
+"""Benchmark of the fused Ulysses QKV path (one JSON line on rank 0).
+
+Workload: the benchmark configurations' model shape (H=4096, Q/KV heads
+32/8, head_dim 128, BF16) with ``world = sp = N`` GPUs (N=4 is configuration
+c1, N=8 is configuration c2; N=1 is the one-GPU self-exchange point) and
+``--tokens`` tokens per GPU (default 4096).  A step is one
+``FlashUlyssesContext.ulysses_qkv_forward`` call; the metric is its device
+latency (max over ranks) and the GEMM-equivalent TFLOP/s per GPU.
+
+Launch: ``python bench.py [--gpus N --steps K --warmup W]``; for N > 1 under
+``torch.distributed.run`` (one process per GPU).  ``--impl reference`` times
+the reference's PyTorch path on the host CPU (the oracle port) instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "fused QKV+exchange latency ms (max rank) vs L; GEMM TFLOP/s/GPU vs peak"
+HIDDEN, Q_HEADS, KV_HEADS, MAX_POS = 4096, 32, 8, 32768
+ROTATE = 4            # distinct input sets cycled per step: 4 x 82 MB > 126 MB L2
+SWEEP = (1, 128, 1024, 4096, 8192)
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--tokens", type=int, default=4096)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return d["bf16_tflops"], d["hbm_gbs"], "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """DRAM bytes per launch of the fused kernel from the committed ncu summary."""
+    path = ROOT / "profiles" / "fused_qkv_exchange_c1shape.md"
+    if not path.exists():
+        return None, None
+    info = {}
+    for line in path.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch_L"):
+            key, val = line.split(":", 1)
+            info[int(key.rsplit("L", 1)[1])] = float(val.strip())
+    return info, path.name
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons with NVML (read-only)."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nvml = None
+
+    def _run(self):
+        n = self.nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM))
+                mask = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                for bit, name in self.REASONS.items():
+                    if mask & bit and bit != 0x1:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.005)
+
+    def start(self):
+        if self.nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join()
+        return {
+            "sm_mhz": statistics.median(self.samples) if self.samples else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(self.reasons),
+            "samples": len(self.samples),
+        }
+
+
+# ---------------------------------------------------------------- helpers
+def max_over_ranks(value, world):
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def rendezvous(world, group=None):
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(group=group)
+
+
+def make_inputs(world, rank, tokens, seed):
+    from flash_ulysses_b200.workloads import make_parameters, make_rank_inputs
+
+    sp = world
+    packed = (Q_HEADS + 2 * KV_HEADS) * 128
+    params = make_parameters(HIDDEN, packed, MAX_POS, tp_rank=0, seed=seed, device="cuda")
+    x, pos = make_rank_inputs(HIDDEN, tokens, MAX_POS, rank=rank, sp_size=sp, seed=seed,
+                              device="cuda")
+    return x, pos, params
+
+
+def time_steps(fn, steps, world, group):
+    """Device time of ``steps`` back-to-back calls bracketed by a barrier and a
+    synchronize on both sides; returns ms per step, max over ranks."""
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    rendezvous(world, group)
+    start.record()
+    for i in range(steps):
+        fn(i)
+    end.record()
+    rendezvous(world, group)
+    return max_over_ranks(start.elapsed_time(end) / steps, world)
+
+
+def time_isolated(fn, steps, world, group):
+    """The reference harness's method (tests/common.py:45-59): rendezvous
+    before every call, CUDA events around one call, mean, max over ranks."""
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    total = 0.0
+    for i in range(steps):
+        rendezvous(world, group)
+        start.record()
+        fn(i)
+        end.record()
+        end.synchronize()
+        total += start.elapsed_time(end)
+    return max_over_ranks(total / steps, world)
+
+
+def torch_reference_step(x, pos, params, sp, group):
+    """The reference's PyTorch path on the GPU (tests/torch_base.py:48-76):
+    cuBLAS projection, separate norm/RoPE kernels, NCCL all_to_all."""
+    widths = (Q_HEADS * 128, KV_HEADS * 128, KV_HEADS * 128)
+    q, k, v = (x @ params["qkv_weight"]).split(widths, dim=-1)
+    cos, sin = params["rope_cache"][pos].unsqueeze(1).chunk(2, dim=-1)
+
+    def norm_rope(t, gamma, eps):
+        value = t.reshape(x.size(0), -1, 128).float()
+        value = value * torch.rsqrt(value.square().mean(dim=-1, keepdim=True) + eps)
+        value = (value * gamma).bfloat16().float()
+        lo, hi = value.chunk(2, dim=-1)
+        return torch.cat((lo * cos - hi * sin, hi * cos + lo * sin), dim=-1).bfloat16().flatten(1)
+
+    q = norm_rope(q, params["q_norm_weight"], params["q_epsilon"])
+    k = norm_rope(k, params["k_norm_weight"], params["k_epsilon"])
+    parts = [t.reshape(x.size(0), sp, -1) for t in (q, k, v)]
+    send = torch.cat(parts, dim=-1).transpose(0, 1).contiguous()
+    if sp == 1:
+        return send
+    received = torch.empty_like(send)
+    dist.all_to_all_single(received, send, group=group)
+    return received
+
+
+# ---------------------------------------------------------------- CPU leg
+def cpu_oracle_time(tokens, sp, budget_s=20.0, steps=None, warmup=1):
+    """One rank's reference PyTorch path on the host cores (the oracle port):
+    projection + norm + RoPE + pack, and the receive-side copy of the
+    exchange.  Returns (ms per step at the full workload, sample description,
+    threads)."""
+    from flash_ulysses_b200.workloads import make_parameters, make_rank_inputs
+    from oracle import ulysses_oracle as oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    packed = (Q_HEADS + 2 * KV_HEADS) * 128
+    topo = oracle.Topology(sp, sp, Q_HEADS, KV_HEADS, HIDDEN)
+    params = make_parameters(HIDDEN, packed, MAX_POS, seed=0)
+
+    def one(n):
+        x, pos = make_rank_inputs(HIDDEN, n, MAX_POS, rank=0, sp_size=sp, seed=0)
+        t0 = time.perf_counter()
+        send = oracle.rank_send(topo, x, pos, params)
+        received = torch.empty_like(send)
+        received.copy_(send)                      # stands in for the all-to-all
+        oracle.unpack(topo, received, n)
+        return time.perf_counter() - t0
+
+    sample = tokens
+    first = one(sample)
+    while first > budget_s / 4 and sample > 128:
+        sample //= 2
+        first = one(sample)
+    n_steps = steps if steps is not None else max(1, min(5, int(budget_s / max(first, 1e-3))))
+    for _ in range(warmup):
+        one(sample)
+    times = [one(sample) for _ in range(n_steps)]
+    per = statistics.mean(times) * tokens / sample * 1e3
+    desc = (f"{n_steps} steps of {sample} of {tokens} tokens/rank, one rank's compute + "
+            f"receive copy, scaled x{tokens / sample:g}")
+    return per, desc, threads
+
+
+def reference_arm(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    tokens, sp = args.tokens, max(args.gpus, world)
+    per, desc, threads = cpu_oracle_time(tokens, sp, budget_s=120.0 / max(args.steps, 1),
+                                         steps=args.steps, warmup=args.warmup)
+    flops = 2 * tokens * HIDDEN * (Q_HEADS + 2 * KV_HEADS) * 128
+    line = {
+        "metric": METRIC, "value": round(per, 4), "unit": "ms", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(per, 4), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": workload_config(args.gpus, tokens),
+        "tflops_per_gpu": round(flops / (per * 1e-3) / 1e12, 3),
+        "cpu_baseline": {"value": round(per, 4), "unit": "ms", "cores": threads,
+                         "kind": "port", "sample": desc},
+        "e2e": {"value": round(per, 4), "unit": "ms", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(n, tokens):
+    return {
+        "workload": f"H={HIDDEN} Q/KV={Q_HEADS}/{KV_HEADS} head_dim=128, world=sp={n} "
+                    f"(c1 shape; N=4 is c1, N=8 is c2), L={tokens} tokens/GPU",
+        "hidden_size": HIDDEN, "num_heads": Q_HEADS, "num_kv_heads": KV_HEADS,
+        "tokens_per_gpu": tokens, "world_size": n, "sp_size": n, "base_tp": 1,
+        "global_tokens": tokens * n,
+        "l2": f"{ROTATE} rotating input sets per rank (>{ROTATE * 82} MB) > 126 MB L2",
+    }
+
+
+# ---------------------------------------------------------------- our arm
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    world, rank, local = dist_env()
+    n = max(world, 1)
+    torch.cuda.set_device(local)
+    group = None
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=__import__("datetime").timedelta(seconds=120))
+        group = dist.new_group(backend="gloo")
+    from flash_ulysses_b200 import FlashUlyssesContext
+
+    tokens = args.tokens
+    max_tokens = max(tokens, max(SWEEP) if not args.no_sweep else tokens)
+    ctx = FlashUlyssesContext(rank=rank, world_size=n, max_local_tokens=max_tokens,
+                              hidden_size=HIDDEN, num_heads=Q_HEADS, num_kv_heads=KV_HEADS,
+                              sp_size=n, control_group=group)
+    sets = [make_inputs(n, rank, tokens, seed=s) for s in range(ROTATE)]
+
+    def step(i):
+        x, pos, p = sets[i % ROTATE]
+        return ctx.ulysses_qkv_forward(x, p["qkv_weight"], pos, p["q_norm_weight"],
+                                       p["k_norm_weight"], p["rope_cache"],
+                                       q_epsilon=p["q_epsilon"], k_epsilon=p["k_epsilon"])
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    # Soak ~0.5 s so the clock record reflects steady load, then time K steps.
+    sampler = ClockSampler(torch.cuda.current_device())
+    sampler.start()
+    t0 = time.perf_counter()
+    i = 0
+    while time.perf_counter() - t0 < 0.5:
+        step(i)
+        i += 1
+        if i % 50 == 0:
+            torch.cuda.synchronize()
+    epoch0 = ctx.epoch
+    ms = time_steps(step, args.steps, n, group)
+    clocks = sampler.stop()
+    launches = ctx.epoch - epoch0
+    ctx.check()
+
+    flops = 2 * tokens * HIDDEN * ctx.packed_width
+    tflops = flops / (ms * 1e-3) / 1e12
+    peak_tf, peak_hbm, peak_src = measured_peaks()
+
+    # The reference harness's per-call method (rendezvous between calls).
+    iso = time_isolated(step, min(args.steps, 20), n, group)
+
+    # e2e: through the public API from pinned host memory, outputs read back.
+    hx = [s[0].cpu().pin_memory() for s in sets]
+    hp = [s[1].cpu().pin_memory() for s in sets]
+    dx = torch.empty_like(sets[0][0])
+    dp = torch.empty_like(sets[0][1])
+    outs_h = [torch.empty((tokens * n, w), dtype=torch.bfloat16).pin_memory()
+              for w in (ctx.output_q_heads * 128, ctx.output_kv_heads * 128,
+                        ctx.output_kv_heads * 128)]
+
+    def e2e_step(i):
+        _, _, p = sets[i % ROTATE]
+        dx.copy_(hx[i % ROTATE], non_blocking=True)
+        dp.copy_(hp[i % ROTATE], non_blocking=True)
+        q, k, v = ctx.ulysses_qkv_forward(dx, p["qkv_weight"], dp, p["q_norm_weight"],
+                                          p["k_norm_weight"], p["rope_cache"],
+                                          q_epsilon=p["q_epsilon"], k_epsilon=p["k_epsilon"])
+        for h, d in zip(outs_h, (q, k, v)):
+            h.copy_(d, non_blocking=True)
+
+    for i in range(2):
+        e2e_step(i)
+    e2e_ms = time_steps(e2e_step, args.steps, n, group)
+    h2d = dx.numel() * 2 + dp.numel() * 8
+    d2h = sum(t.numel() * 2 for t in outs_h)
+
+    # The reference's own PyTorch + NCCL path on the same GPUs.
+    def torch_step(i):
+        x, pos, p = sets[i % ROTATE]
+        torch_reference_step(x, pos, p, n, None)
+
+    for i in range(2):
+        torch_step(i)
+    torch_ms = time_steps(torch_step, min(args.steps, 20), n, group)
+
+    sweep = {}
+    if not args.no_sweep:
+        for L in SWEEP:
+            s_sets = sets if L == tokens else [make_inputs(n, rank, L, seed=s)
+                                               for s in range(ROTATE)]
+
+            def s_step(i, s_sets=s_sets):
+                x, pos, p = s_sets[i % ROTATE]
+                ctx.ulysses_qkv_forward(x, p["qkv_weight"], pos, p["q_norm_weight"],
+                                        p["k_norm_weight"], p["rope_cache"],
+                                        q_epsilon=p["q_epsilon"], k_epsilon=p["k_epsilon"])
+
+            for i in range(3):
+                s_step(i)
+            t = time_steps(s_step, 20, n, group)
+            f = 2 * L * HIDDEN * ctx.packed_width
+            sweep[str(L)] = {"ms": round(t, 5), "tflops_per_gpu": round(f / (t * 1e-3) / 1e12, 1)}
+            del s_sets
+        ctx.check()
+
+    cpu = None
+    if rank == 0 and n == 1 and not args.no_cpu_baseline:
+        per, desc, threads = cpu_oracle_time(tokens, n)
+        cpu = {"value": round(per, 3), "unit": "ms", "cores": threads, "kind": "port",
+               "sample": desc}
+
+    traffic_map, traffic_src = profiled_traffic()
+    traffic = None if not traffic_map else traffic_map.get(tokens)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(ms, 5), "unit": "ms", "n_gpus": n,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded N(0,1) activations, N(0,H^-1/2) "
+                                     "weights, random-init; no checkpoint)",
+            "config": workload_config(n, tokens),
+            "tflops_per_gpu": round(tflops, 1),
+            "frac_of_peak_bf16": round(tflops / peak_tf, 4),
+            "tokens_per_s_total": round(tokens * n / (ms * 1e-3), 1),
+            "latency_ms_isolated": round(iso, 5),
+            "torch_gpu_path_ms": round(torch_ms, 5),
+            "speedup_vs_torch_gpu_path": round(torch_ms / ms, 3),
+            "latency_ms_by_tokens": sweep,
+            "roofline": {
+                "bound": "tensor", "achieved": round(tflops, 1), "peak": peak_tf,
+                "unit": "TFLOP/s", "frac": round(tflops / peak_tf, 4),
+                "peak_source": f"{peak_src} bf16 burst (MEASURED_PEAKS.json)",
+                "traffic": traffic, "traffic_source": traffic_src,
+            },
+            "clocks": clocks,
+            "e2e": {"value": round(e2e_ms, 5), "unit": "ms", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group(group)
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

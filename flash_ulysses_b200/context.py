@@ -56,7 +56,6 @@ class FlashUlyssesContext:
         self.num_heads, self.num_kv_heads = num_heads, num_kv_heads
         self.head_dim, self.sp_size = head_dim, sp_size
         self.max_local_tokens = max_local_tokens
-        self.device = torch.device("cuda", torch.cuda.current_device())
         self._op = None
         self._status = None
         self.Q = self.K = self.V = self.barrier = None
@@ -75,6 +74,9 @@ class FlashUlyssesContext:
             raise ValueError("Q heads must divide by KV heads; both must divide by world_size")
         if max_local_tokens <= 0:
             raise ValueError("max_local_tokens must be positive")
+        if not 0 <= rank < world_size:
+            raise ValueError("rank must be in [0, world_size)")
+        self.device = torch.device("cuda", torch.cuda.current_device())
         if torch.cuda.get_device_capability(self.device) != (10, 0):
             raise ValueError("Requires SM100 (B200)")
 
