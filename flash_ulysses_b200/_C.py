@@ -37,7 +37,7 @@ EXPORTED = (
     "fu_buffer_alloc", "fu_buffer_free", "fu_buffer_export", "fu_buffer_import",
     "fu_buffer_close", "fu_status_alloc", "fu_status_free",
     "fu_qkv_create", "fu_qkv_destroy", "fu_qkv_forward", "fu_qkv_epoch",
-    "fu_qkv_last_grid",
+    "fu_qkv_last_grid", "fu_qkv_forward_noalloc",
 )
 
 
@@ -86,12 +86,14 @@ def _load():
                                           ctypes.c_double, ctypes.c_double, u32, vp, vp]),
         "fu_qkv_epoch": (u32, [vp]),
         "fu_qkv_last_grid": (ctypes.c_int, [vp]),
+        "fu_qkv_forward_noalloc": (ctypes.c_int, [ctypes.c_int, vp, vp, vp, vp, vp, vp, i64, i64,
+                                                  i32, i32, i64, ctypes.c_double,
+                                                  ctypes.c_double, vp, vp, vp, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
         fn.restype = res
         fn.argtypes = args
-    del i32
     return lib
 
 

@@ -684,3 +684,183 @@ extern "C" int fu_qkv_forward(fu_qkv_ctx* ctx, const void* x, const void* w,
     if (e != cudaSuccess) return set_error(FU_ERR_CUDA, "launch failed: %s", cudaGetErrorString(e));
     return FU_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point (one GPU).
+//
+// Some callers cannot allocate device memory where they call this operator:
+// an inference server that reserves all free HBM for its KV cache up front and
+// hands out memory only through its own pool, an embedding runtime whose
+// allocator is not CUDA's, or a plain C caller that owns only the buffers it
+// passes in.  For them, fu_qkv_forward_noalloc runs the same fused kernel for a
+// world of one GPU (self-exchange) with every byte of its scratch -- the CTA
+// completion counter and the exit flag -- in the file-scope array below, so
+// the call itself allocates nothing: no cudaMalloc, cudaFree, cudaHostAlloc or
+// allocating library routine, on any call.
+namespace fu {
+// Scratch of the allocation-free entry point: FU_SYNC_WORDS 32-bit words
+// (256 bytes), laid out like a per-rank sync block.  Every GPU that loads this
+// library holds it until the process exits.  Calls share it and it keeps the
+// previous call's contents: each call zeroes the completion counter first, and
+// calls that overlap on the same GPU (for example on two streams) race on it.
+static __device__ __align__(256) uint32_t g_noalloc_scratch[FU_SYNC_WORDS];
+
+constexpr int kNoallocMaxDevices = 64;
+
+struct NoallocDevice {
+    std::once_flag once;
+    int rc = FU_OK;
+    char message[256] = {0};
+    uint32_t* scratch = nullptr;     // device address of g_noalloc_scratch
+    int sm_count = 0;
+    uint32_t epoch = 0;
+};
+static NoallocDevice g_noalloc_devices[kNoallocMaxDevices];
+
+// Once per device, with that device current: resolve the scratch array's
+// device address (host code may not use the symbol itself as an address) and
+// raise the kernel's shared-memory limit.
+static void noalloc_setup(int device, NoallocDevice& st) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+        st.rc = FU_ERR_CUDA;
+        snprintf(st.message, sizeof(st.message), "cudaGetSymbolAddress(scratch) on device %d: %s",
+                 device, cudaGetErrorString(e));
+        return;
+    }
+    e = cudaFuncSetAttribute(fused_qkv_exchange_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount,
+                                                     device);
+    if (e != cudaSuccess) {
+        st.rc = FU_ERR_CUDA;
+        snprintf(st.message, sizeof(st.message), "set-up on device %d: %s", device,
+                 cudaGetErrorString(e));
+        return;
+    }
+    st.scratch = static_cast<uint32_t*>(ptr);
+}
+}  // namespace fu
+
+extern "C" int fu_qkv_forward_noalloc(int device, const void* x, const void* w,
+                                      const int64_t* positions, const float* q_gamma,
+                                      const float* k_gamma, const float* rope,
+                                      int64_t local_tokens, int64_t hidden_size, int32_t q_heads,
+                                      int32_t kv_heads, int64_t rope_rows, double q_epsilon,
+                                      double k_epsilon, void* q_out, void* k_out, void* v_out,
+                                      int32_t* status, void* stream) {
+    const int64_t L = local_tokens;
+    if (device < 0 || device >= kNoallocMaxDevices)
+        return set_error(FU_ERR_INVALID, "device %d outside [0, %d)", device, kNoallocMaxDevices);
+    if (L < 1 || L > FU_NOALLOC_MAX_TOKENS)
+        return set_error(FU_ERR_INVALID,
+                         "local_tokens %lld outside [1, %d], the largest count the kernel's "
+                         "32-bit row indices and the fixed scratch serve",
+                         static_cast<long long>(L), FU_NOALLOC_MAX_TOKENS);
+    if (hidden_size <= 0 || hidden_size % 64 || hidden_size > (int64_t(1) << 30))
+        return set_error(FU_ERR_INVALID, "hidden_size %lld must be a positive multiple of 64",
+                         static_cast<long long>(hidden_size));
+    if (q_heads <= 0 || kv_heads <= 0 || q_heads > 4096 || kv_heads > 4096)
+        return set_error(FU_ERR_INVALID, "head counts (%d, %d) out of range", q_heads, kv_heads);
+    if (!x || !w || !positions || !q_gamma || !k_gamma || !rope || !q_out || !k_out || !v_out)
+        return set_error(FU_ERR_INVALID, "null pointer argument");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
+         reinterpret_cast<uintptr_t>(rope) | reinterpret_cast<uintptr_t>(q_out) |
+         reinterpret_cast<uintptr_t>(k_out) | reinterpret_cast<uintptr_t>(v_out)) & 15)
+        return set_error(FU_ERR_INVALID, "x, w, rope and the outputs must be 16-byte aligned");
+    if (rope_rows < 1) return set_error(FU_ERR_INVALID, "rope_rows must be positive");
+
+    int prev = 0;
+    if (cudaGetDevice(&prev) != cudaSuccess) return set_error(FU_ERR_CUDA, "cudaGetDevice failed");
+    if (prev != device && cudaSetDevice(device) != cudaSuccess)
+        return set_error(FU_ERR_INVALID, "device %d is not available", device);
+    struct Restore {
+        int prev, dev;
+        ~Restore() { if (prev != dev) cudaSetDevice(prev); }
+    } restore{prev, device};
+
+    NoallocDevice& st = g_noalloc_devices[device];
+    std::call_once(st.once, [&] {
+        int major = 0, minor = 0;
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+        if (major != 10 || minor != 0) {
+            st.rc = FU_ERR_UNSUPPORTED;
+            snprintf(st.message, sizeof(st.message), "requires an sm_100 GPU; device %d is sm_%d%d",
+                     device, major, minor);
+            return;
+        }
+        noalloc_setup(device, st);
+    });
+    if (st.rc != FU_OK) return set_error(st.rc, "%s", st.message);
+
+    // Parameters live on the host stack; the launch copies them.
+    QkvParams p;
+    std::memset(&p, 0, sizeof(p));
+    const int heads = q_heads + 2 * kv_heads;
+    const int64_t N = static_cast<int64_t>(heads) * FU_HEAD_DIM;
+    int rc;
+    {
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(hidden_size), static_cast<cuuint64_t>(L)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(hidden_size * 2)};
+        const cuuint32_t box[2] = {BK, BM};
+        if ((rc = encode(&p.tm_x, x, 2, dims, strides, box, "hidden_states")) != FU_OK) return rc;
+    }
+    {
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(hidden_size)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(N * 2)};
+        const cuuint32_t box[2] = {64, BK};
+        if ((rc = encode(&p.tm_w, w, 2, dims, strides, box, "qkv_weight")) != FU_OK) return rc;
+    }
+    void* outs[3] = {q_out, k_out, v_out};
+    for (int comp = 0; comp < 3; ++comp) {
+        const int64_t cols = static_cast<int64_t>(comp == 0 ? q_heads : kv_heads) * FU_HEAD_DIM;
+        const cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(L), 1};
+        const cuuint64_t strides[2] = {static_cast<cuuint64_t>(cols * 2),
+                                       static_cast<cuuint64_t>(L * cols * 2)};
+        const cuuint32_t box[3] = {64, 32, 1};
+        if ((rc = encode(&p.tm_out[comp * FU_MAX_SP], outs[comp], 3, dims, strides, box,
+                         "output")) != FU_OK)
+            return rc;
+    }
+    p.positions = positions;
+    p.q_gamma = q_gamma;
+    p.k_gamma = k_gamma;
+    p.rope = rope;
+    p.gemm_out = nullptr;
+    p.sync[0] = st.scratch;
+    p.status = status;
+    p.timeout_ns = 5000000000ull;
+    p.L = static_cast<int32_t>(L);
+    p.H = static_cast<int32_t>(hidden_size);
+    p.N = static_cast<int32_t>(N);
+    p.rope_rows = rope_rows > INT32_MAX ? INT32_MAX : static_cast<int32_t>(rope_rows);
+    p.heads = heads;
+    p.q_heads = q_heads;
+    p.kv_heads = kv_heads;
+    p.sp_size = 1;
+    p.sp_rank = 0;
+    p.q_per_gpu = q_heads;
+    p.kv_per_gpu = kv_heads;
+    p.num_n_blocks = (heads + 1) / 2;
+    const int64_t tiles = (L + BM - 1) / BM * p.num_n_blocks;
+    p.num_tiles = static_cast<int32_t>(tiles);
+    p.k_blocks = static_cast<int32_t>(hidden_size / BK);
+    p.q_eps = static_cast<float>(q_epsilon);
+    p.k_eps = static_cast<float>(k_epsilon);
+    // Any epoch works for a world of one: the kernel publishes its own flag
+    // before it reads it.  Only the completion counter must start at zero.
+    p.epoch = ++st.epoch;
+    if (p.epoch == 0) p.epoch = ++st.epoch;
+    p.wait_peers = 1u;
+
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemsetAsync(st.scratch + FU_SYNC_COUNTER, 0, sizeof(uint32_t), s);
+    if (e != cudaSuccess) return set_error(FU_ERR_CUDA, "clearing scratch: %s", cudaGetErrorString(e));
+    const int grid = static_cast<int>(tiles < st.sm_count ? tiles : st.sm_count);
+    fused_qkv_exchange_kernel<<<grid, NUM_THREADS, SMEM_ALLOC, s>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(FU_ERR_CUDA, "launch failed: %s", cudaGetErrorString(e));
+    return FU_OK;
+}

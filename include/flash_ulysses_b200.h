@@ -155,6 +155,33 @@ FU_API uint32_t fu_qkv_epoch(const fu_qkv_ctx* ctx);
 /* Number of CTAs the most recent call launched (persistent grid). */
 FU_API int fu_qkv_last_grid(const fu_qkv_ctx* ctx);
 
+/* ------------------------------------------------------------------------
+ * Allocation-free call for a world of one GPU.  This entry point has no
+ * counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory where they call the
+ * operator -- e.g. a server that has reserved all free HBM for its own pool,
+ * or a C caller that owns only the buffers it passes in.  It runs the same
+ * fused kernel as fu_qkv_forward with sp_size 1 (outputs Q [L, q_heads*128],
+ * K and V [L, kv_heads*128], BF16 row-major) and allocates nothing on any
+ * call: its scratch (completion counter and exit flag, FU_SYNC_WORDS words =
+ * 256 bytes) is a static array inside the library that every GPU loading the
+ * library holds until the process exits.  The first call on a device resolves
+ * that array's address and sets the kernel's shared-memory limit; make that
+ * first call before any stream capture.  Calls share the scratch and each one
+ * zeroes the counter before launching, so calls that overlap on the same GPU
+ * race.  Rejects local_tokens outside [1, FU_NOALLOC_MAX_TOKENS].
+ * `status` is an optional caller-owned device int32 that receives a device-side
+ * status code (NULL: not reported).  No context object is needed. */
+#define FU_NOALLOC_MAX_TOKENS (1 << 30)
+FU_API int fu_qkv_forward_noalloc(int device, const void* x, const void* w,
+                                  const int64_t* positions, const float* q_gamma,
+                                  const float* k_gamma, const float* rope,
+                                  int64_t local_tokens, int64_t hidden_size, int32_t q_heads,
+                                  int32_t kv_heads, int64_t rope_rows, double q_epsilon,
+                                  double k_epsilon, void* q_out, void* k_out, void* v_out,
+                                  int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
