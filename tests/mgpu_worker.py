@@ -1,0 +1,237 @@
+"""Multi-GPU worker for tests/test_gpu_multi.py (one process per GPU, launched
+with torch.distributed.run).
+
+For every case it builds a FlashUlyssesContext over real CUDA IPC mappings and
+checks this rank's outputs against the reference's PyTorch path run on the
+GPUs (oracle restatement on CUDA tensors + NCCL all_to_all_single inside the
+SP group, tests/torch_base.py:48-76) and, for small cases, against the CPU
+oracle.  Placement, padding and untouched capacity are checked bit for bit on
+exact inputs.  Then back-to-back calls without a host rendezvous, and finally
+a host-side fault: one rank skips a call and its peers' bounded wait must
+report it.
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+import sys
+import traceback
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+from flash_ulysses_b200 import FlashUlyssesContext  # noqa: E402
+from flash_ulysses_b200.workloads import Config, make_world  # noqa: E402
+from oracle import ulysses_oracle as oracle  # noqa: E402
+
+ATOL = RTOL = 0.01
+
+
+def log(msg):
+    if dist.get_rank() == 0:
+        print(msg, flush=True)
+
+
+def sp_groups(world, sp, backend):
+    mine = None
+    for start in range(0, world, sp):
+        g = dist.new_group(list(range(start, start + sp)), backend=backend)
+        if start <= dist.get_rank() < start + sp:
+            mine = g
+    return mine
+
+
+def reference_gpu(topo, x, pos, params, group):
+    """The reference's PyTorch path on this GPU (cuBLAS + NCCL)."""
+    send = oracle.rank_send(topo, x, pos, params)
+    if topo.sp_size == 1:
+        return oracle.unpack(topo, send, x.size(0))
+    received = torch.empty_like(send)
+    dist.all_to_all_single(received, send, group=group)
+    return oracle.unpack(topo, received, x.size(0))
+
+
+def run_case(cfg, tokens_list, gloo, *, cpu_check_max=256):
+    rank, world = dist.get_rank(), dist.get_world_size()
+    topo = oracle.Topology(cfg.world_size, cfg.sp_size, cfg.num_heads, cfg.num_kv_heads,
+                           cfg.hidden_size)
+    nccl_sp = sp_groups(world, cfg.sp_size, "nccl")
+    ctx = FlashUlyssesContext(rank=rank, world_size=world, max_local_tokens=max(tokens_list) + 5,
+                              hidden_size=cfg.hidden_size, num_heads=cfg.num_heads,
+                              num_kv_heads=cfg.num_kv_heads, sp_size=cfg.sp_size,
+                              control_group=gloo, timeout_s=10.0)
+    failures = []
+    try:
+        for tokens in tokens_list:
+            xs, pos, params = make_world(cfg, tokens, seed=tokens)
+            dev = torch.device("cuda", torch.cuda.current_device())
+            gp = {k: (v.to(dev) if torch.is_tensor(v) else v) for k, v in params[rank].items()}
+            x, p = xs[rank].to(dev), pos[rank].to(dev)
+            for t in (ctx.Q, ctx.K, ctx.V):
+                t.data_.fill_(float("nan"))
+            torch.cuda.synchronize()
+            dist.barrier(group=gloo)
+            got = ctx.ulysses_qkv_forward(x, gp["qkv_weight"], p, gp["q_norm_weight"],
+                                          gp["k_norm_weight"], gp["rope_cache"],
+                                          q_epsilon=gp["q_epsilon"], k_epsilon=gp["k_epsilon"])
+            ctx.check()
+            want = reference_gpu(topo, x, p, gp, nccl_sp)
+            stats = []
+            total_bad = 0
+            for g, w, name in zip(got, want, "QKV"):
+                bad = int((~torch.isclose(g.float(), w.float(), atol=ATOL, rtol=RTOL)).sum())
+                err = float((g.float() - w.float()).abs().max())
+                total_bad += bad
+                stats.append(f"{name} viol {bad} max {err:.3g}")
+                if bad and err > 0.0625:
+                    failures.append(f"{cfg.name} L={tokens} {name}: max err {err}")
+            numel = sum(g.numel() for g in got)
+            if total_bad > max(1, 2e-6 * numel):
+                failures.append(f"{cfg.name} L={tokens}: {total_bad} violations vs GPU reference")
+            if tokens <= cpu_check_max:
+                cpu = oracle.simulate_world(topo, xs, pos, params)[rank]
+                for g, w, name in zip(got, cpu, "QKV"):
+                    bad = int((~torch.isclose(g.float().cpu(), w.float(), atol=ATOL,
+                                              rtol=RTOL)).sum())
+                    if bad > max(1, 2e-6 * g.numel()):
+                        failures.append(f"{cfg.name} L={tokens} {name}: {bad} vs CPU oracle")
+            rows = tokens * cfg.sp_size
+            for t, name in zip((ctx.Q, ctx.K, ctx.V), "QKV"):
+                if not bool(torch.isnan(t.data_[rows:].float()).all()):
+                    failures.append(f"{cfg.name} L={tokens} {name}: capacity written")
+            log(f"  {cfg.name} P={world} S={cfg.sp_size} L={tokens}: " + ", ".join(stats))
+
+        # Back-to-back calls without host rendezvous; the last one is checked.
+        tokens = tokens_list[-1]
+        xs, pos, params = make_world(cfg, tokens, seed=99)
+        gp = {k: (v.cuda() if torch.is_tensor(v) else v) for k, v in params[rank].items()}
+        x, p = xs[rank].cuda(), pos[rank].cuda()
+        dist.barrier(group=gloo)
+        for _ in range(20):
+            got = ctx.ulysses_qkv_forward(x, gp["qkv_weight"], p, gp["q_norm_weight"],
+                                          gp["k_norm_weight"], gp["rope_cache"],
+                                          q_epsilon=gp["q_epsilon"], k_epsilon=gp["k_epsilon"])
+        ctx.check()
+        want = reference_gpu(topo, x, p, gp, nccl_sp)
+        for g, w, name in zip(got, want, "QKV"):
+            bad = int((~torch.isclose(g.float(), w.float(), atol=ATOL, rtol=RTOL)).sum())
+            if bad > max(1, 2e-6 * g.numel()):
+                failures.append(f"{cfg.name} back-to-back {name}: {bad} violations")
+    finally:
+        dist.barrier(group=gloo)
+        ctx.close()
+    return failures
+
+
+def exact_placement_case(world, sp, gloo):
+    """Bit-exact placement/padding/capacity on exact inputs over real peer memory."""
+    from test_gpu_kernel import exact_world
+
+    rank = dist.get_rank()
+    T = world // sp
+    q_local, kv_local, H, tokens = 4 * sp, 2 * sp, 256, 67
+    xs, pos, params = exact_world(sp, H, q_local, kv_local, tokens)
+    topo = oracle.Topology(sp, sp, q_local, kv_local, H)
+    want = oracle.simulate_world(topo, xs, pos, params)
+    ctx = FlashUlyssesContext(rank=rank, world_size=world, max_local_tokens=tokens + 9,
+                              hidden_size=H, num_heads=q_local * T, num_kv_heads=kv_local * T,
+                              sp_size=sp, control_group=gloo)
+    failures = []
+    try:
+        for t in (ctx.Q, ctx.K, ctx.V):
+            t.data_.fill_(float("nan"))
+        torch.cuda.synchronize()
+        dist.barrier(group=gloo)
+        r = rank % sp
+        gp = {k: (v.cuda() if torch.is_tensor(v) else v) for k, v in params[r].items()}
+        ctx.ulysses_qkv_forward(xs[r].cuda(), gp["qkv_weight"], pos[r].cuda(),
+                                gp["q_norm_weight"], gp["k_norm_weight"], gp["rope_cache"],
+                                q_epsilon=gp["q_epsilon"], k_epsilon=gp["k_epsilon"])
+        ctx.check()
+        rows = tokens * sp
+        for c, t in enumerate((ctx.Q, ctx.K, ctx.V)):
+            full = t.data_.cpu()
+            if not torch.equal(full[:rows].view(torch.int16), want[r][c].view(torch.int16)):
+                failures.append(f"exact P={world} S={sp}: component {c} differs")
+            if not bool(torch.isnan(full[rows:].float()).all()):
+                failures.append(f"exact P={world} S={sp}: capacity written")
+        log(f"  exact placement P={world} S={sp}: {'ok' if not failures else failures}")
+    finally:
+        dist.barrier(group=gloo)
+        ctx.close()
+    return failures
+
+
+def fault_case(gloo):
+    """A rank that never joins a call: the others' bounded wait reports it and
+    the host raises, without hanging or faulting the GPU."""
+    rank, world = dist.get_rank(), dist.get_world_size()
+    cfg = Config("fault", world, world, 1024, 8 * world, 2 * world, (16,), 4096)
+    ctx = FlashUlyssesContext(rank=rank, world_size=world, max_local_tokens=16,
+                              hidden_size=1024, num_heads=8 * world, num_kv_heads=2 * world,
+                              sp_size=world, control_group=gloo, timeout_s=0.2)
+    failures = []
+    try:
+        xs, pos, params = make_world(cfg, 16, seed=5)
+        gp = {k: (v.cuda() if torch.is_tensor(v) else v) for k, v in params[rank].items()}
+        dist.barrier(group=gloo)
+        if rank != world - 1:          # the last rank skips this call
+            ctx.ulysses_qkv_forward(xs[rank].cuda(), gp["qkv_weight"], pos[rank].cuda(),
+                                    gp["q_norm_weight"], gp["k_norm_weight"], gp["rope_cache"])
+            try:
+                ctx.check()
+                failures.append(f"rank {rank}: missing peer not detected")
+            except RuntimeError as e:
+                if "peer flag wait timed out" not in str(e):
+                    failures.append(f"rank {rank}: unexpected error {e}")
+        log(f"  fault injection (rank {world - 1} skips a call): "
+            f"{'detected' if not failures else failures}")
+    finally:
+        dist.barrier(group=gloo)
+        ctx.close()
+    return failures
+
+
+def main():
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                            timeout=datetime.timedelta(seconds=120))
+    gloo = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=120))
+    world = dist.get_world_size()
+    torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+    base = (4096, 32, 8)
+    cases = [Config(f"P{world}S{world}", world, world, *base, (1, 65, 129, 1024), 32768)]
+    if world >= 4:
+        cases.append(Config(f"P{world}S{world // 2}", world, world // 2, *base, (1, 129, 512),
+                            32768))
+    if world == 8:
+        cases.append(Config("c3", 8, 4, 4096, 32, 8, (1, 16, 64, 129, 512), 32768))
+        cases.append(Config("c4", 8, 8, 5120, 64, 8, (8192,), 131072))
+    failures = []
+    try:
+        for cfg in cases:
+            failures += run_case(cfg, list(cfg.tokens), gloo)
+        failures += exact_placement_case(world, world, gloo)
+        if world >= 4:
+            failures += exact_placement_case(world, world // 2, gloo)
+        failures += fault_case(gloo)
+    except Exception:
+        failures.append(f"rank {dist.get_rank()}: " + traceback.format_exc())
+    flag = torch.tensor([len(failures)], device="cuda")
+    dist.all_reduce(flag)
+    if failures:
+        print(f"rank {dist.get_rank()} FAILURES: {failures}", flush=True)
+    log(f"MULTI-GPU RESULT world={world}: {'PASS' if int(flag.item()) == 0 else 'FAIL'}")
+    dist.destroy_process_group(gloo)
+    dist.destroy_process_group()
+    sys.exit(0 if int(flag.item()) == 0 else 1)
+
+
+if __name__ == "__main__":
+    main()
