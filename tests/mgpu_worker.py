@@ -94,12 +94,19 @@ def run_case(cfg, tokens_list, gloo, *, cpu_check_max=256):
             if total_bad > max(1, 2e-6 * numel):
                 failures.append(f"{cfg.name} L={tokens}: {total_bad} violations vs GPU reference")
             if tokens <= cpu_check_max:
+                # Against the CPU oracle, the kernel may be no further off than the
+                # reference's own GPU path is (both differ from the CPU only by the
+                # FP32 accumulation order of the projection).
                 cpu = oracle.simulate_world(topo, xs, pos, params)[rank]
-                for g, w, name in zip(got, cpu, "QKV"):
+                for g, w, ref, name in zip(got, cpu, want, "QKV"):
                     bad = int((~torch.isclose(g.float().cpu(), w.float(), atol=ATOL,
                                               rtol=RTOL)).sum())
-                    if bad > max(1, 2e-6 * g.numel()):
-                        failures.append(f"{cfg.name} L={tokens} {name}: {bad} vs CPU oracle")
+                    ref_bad = int((~torch.isclose(ref.float().cpu(), w.float(), atol=ATOL,
+                                                  rtol=RTOL)).sum())
+                    stats.append(f"{name} vs CPU {bad} (GPU ref vs CPU {ref_bad})")
+                    if bad > ref_bad + max(1, 2e-6 * g.numel()):
+                        failures.append(f"{cfg.name} L={tokens} {name}: {bad} vs CPU oracle "
+                                        f"(reference GPU path: {ref_bad})")
             rows = tokens * cfg.sp_size
             for t, name in zip((ctx.Q, ctx.K, ctx.V), "QKV"):
                 if not bool(torch.isnan(t.data_[rows:].float()).all()):
