@@ -388,7 +388,10 @@ def main():
                 s_step(i)
             t = time_steps(s_step, 20, n, group)
             f = 2 * L * HIDDEN * ctx.packed_width
-            sweep[str(L)] = {"ms": round(t, 5), "tflops_per_gpu": round(f / (t * 1e-3) / 1e12, 1)}
+            sweep[str(L)] = {"ms": round(t, 5), "tflops_per_gpu": round(f / (t * 1e-3) / 1e12, 1),
+                             "grid": ctx._op.last_grid,
+                             "weight_read_gbs": round(HIDDEN * ctx.packed_width * 2 / (t * 1e-3)
+                                                      / 1e9, 1)}
             del s_sets
         ctx.check()
 

@@ -22,6 +22,11 @@ FU_SYNC_WORDS = 64
 FU_SYNC_COUNTER = 32
 FU_FWD_NO_PEER_WAIT = 1
 
+
+def FU_FWD_SPLITS(n):
+    """Flag bits forcing the split-K factor (0 = automatic)."""
+    return (n & 0xF) << 8
+
 FU_OK, FU_ERR_INVALID, FU_ERR_CUDA, FU_ERR_UNSUPPORTED, FU_ERR_DEVICE = range(5)
 STATUS_NAMES = {
     0: "ok",
@@ -30,7 +35,10 @@ STATUS_NAMES = {
     3: "position outside rope_cache",
 }
 
-LIB_PATH = Path(__file__).resolve().parent / "libflash_ulysses_b200.so"
+# FLASH_ULYSSES_B200_LIB points at a library built elsewhere (e.g. a system
+# install); by default the in-tree build is used.
+LIB_PATH = Path(os.environ.get("FLASH_ULYSSES_B200_LIB",
+                               Path(__file__).resolve().parent / "libflash_ulysses_b200.so"))
 
 EXPORTED = (
     "fu_last_error", "fu_version",

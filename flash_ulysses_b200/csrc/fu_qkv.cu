@@ -62,6 +62,10 @@ constexpr int NUM_BARS = 2 * STAGES + 2 + 2 + 1;
 constexpr int OFF_MISC = OFF_BAR + 128;
 constexpr int OFF_GAMMA = OFF_MISC + 64;
 constexpr int SMEM_BYTES = OFF_GAMMA + 2 * 128 * 4;
+// Split mode parks a 128 x 256 FP32 partial in the operand ring; rows are
+// padded by 16 bytes so that a warp's row-per-thread stores spread over banks.
+constexpr int PART_STRIDE = BN * 4 + 16;
+static_assert(BM * PART_STRIDE <= OFF_STG, "split partial must fit in the operand ring");
 constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;                 // room to align the base to 1 KiB
 static_assert(NUM_BARS * 8 <= 128, "barrier area");
 static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KiB per-CTA shared memory limit");
@@ -88,6 +92,8 @@ struct __align__(64) QkvParams {
     float q_eps, k_eps;
     uint32_t epoch;
     uint32_t wait_peers;
+    int32_t splits;                         // >1: split-K over a cluster of this many CTAs
+    void* out_base[3 * FU_MAX_SP];          // receive buffers (split mode stores rows directly)
 };
 static_assert(sizeof(QkvParams) <= 4096, "kernel parameter block too large");
 
@@ -119,9 +125,38 @@ __device__ __forceinline__ bool drain_wait(uint32_t bar, uint32_t parity, uint64
     return true;
 }
 
+// ------------------------------------------------------------ schedule
+// Which tiles and which k-blocks this CTA owns.  Persistent mode (splits 1):
+// tiles blockIdx.x, +gridDim.x, ... over the full reduction.  Split mode:
+// the CTAs of one cluster share one tile; cluster rank s reduces k-blocks
+// [s*KB/S, (s+1)*KB/S).
+struct Sched {
+    int first, end, stride, kb0, kb1, split;
+};
+
+__device__ __forceinline__ Sched make_sched(const QkvParams& p) {
+    Sched s;
+    if (p.splits > 1) {
+        s.split = static_cast<int>(blockIdx.x) % p.splits;
+        s.first = static_cast<int>(blockIdx.x) / p.splits;
+        s.end = s.first + 1;
+        s.stride = 1;
+        s.kb0 = s.split * p.k_blocks / p.splits;
+        s.kb1 = (s.split + 1) * p.k_blocks / p.splits;
+    } else {
+        s.split = 0;
+        s.first = blockIdx.x;
+        s.end = p.num_tiles;
+        s.stride = gridDim.x;
+        s.kb0 = 0;
+        s.kb1 = p.k_blocks;
+    }
+    return s;
+}
+
 // ------------------------------------------------------------ roles
-__device__ void run_producer(const QkvParams& p, uint8_t* smem, uint32_t bar_full,
-                             uint32_t bar_empty, volatile int* abort_flag) {
+__device__ void run_producer(const QkvParams& p, const Sched& sc, uint8_t* smem,
+                             uint32_t bar_full, uint32_t bar_empty, volatile int* abort_flag) {
     int stage = 0;
     uint32_t phase = 0;
     uint32_t issued_mask = 0;               // stages loaded at least once
@@ -129,10 +164,10 @@ __device__ void run_producer(const QkvParams& p, uint8_t* smem, uint32_t bar_ful
     const uint32_t a0 = smem_u32(smem + OFF_A);
     const uint32_t b0 = smem_u32(smem + OFF_B);
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+    for (int tile = sc.first; ok && tile < sc.end; tile += sc.stride) {
         const int m_blk = tile / p.num_n_blocks;
         const int n_blk = tile % p.num_n_blocks;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = sc.kb0; kb < sc.kb1; ++kb) {
             if (!fu_wait_parity(bar_empty + 8 * stage, phase ^ 1u, abort_flag, p.timeout_ns,
                                 p.status, W_EMPTY)) {
                 ok = false;
@@ -161,9 +196,9 @@ __device__ void run_producer(const QkvParams& p, uint8_t* smem, uint32_t bar_ful
     }
 }
 
-__device__ void run_mma(const QkvParams& p, uint8_t* smem, uint32_t tmem_base, uint32_t bar_full,
-                        uint32_t bar_empty, uint32_t bar_tfull, uint32_t bar_tempty,
-                        uint32_t bar_mma_done, volatile int* abort_flag) {
+__device__ void run_mma(const QkvParams& p, const Sched& sc, uint8_t* smem, uint32_t tmem_base,
+                        uint32_t bar_full, uint32_t bar_empty, uint32_t bar_tfull,
+                        uint32_t bar_tempty, uint32_t bar_mma_done, volatile int* abort_flag) {
     constexpr uint32_t idesc = make_idesc_bf16_f32(BM, BN, /*a_mn_major=*/false,
                                                    /*b_mn_major=*/true);
     const uint32_t a0 = smem_u32(smem + OFF_A);
@@ -172,7 +207,7 @@ __device__ void run_mma(const QkvParams& p, uint8_t* smem, uint32_t tmem_base, u
     uint32_t phase = 0;
     int local = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++local) {
+    for (int tile = sc.first; ok && tile < sc.end; tile += sc.stride, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!fu_wait_parity(bar_tempty + 8 * acc, acc_phase ^ 1u, abort_flag, p.timeout_ns,
@@ -182,7 +217,7 @@ __device__ void run_mma(const QkvParams& p, uint8_t* smem, uint32_t tmem_base, u
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = sc.kb0; kb < sc.kb1; ++kb) {
             if (!fu_wait_parity(bar_full + 8 * stage, phase, abort_flag, p.timeout_ns, p.status,
                                 W_FULL)) {
                 ok = false;
@@ -199,7 +234,7 @@ __device__ void run_mma(const QkvParams& p, uint8_t* smem, uint32_t tmem_base, u
                 // (leading offset), 8-row groups 1024 bytes apart (stride offset).
                 const uint64_t bdesc =
                     make_smem_desc_sw128(b_base + k * UMMA_K * 128, B_CHUNK_BYTES, 1024);
-                tc_mma_bf16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+                tc_mma_bf16(d_tmem, adesc, bdesc, idesc, (kb != sc.kb0 || k != 0) ? 1u : 0u);
             }
             tc_commit(bar_empty + 8 * stage);      // frees the stage when these MMAs finish
             if (++stage == STAGES) {
@@ -214,162 +249,336 @@ __device__ void run_mma(const QkvParams& p, uint8_t* smem, uint32_t tmem_base, u
     drain_wait(bar_mma_done, 0, p.timeout_ns, p.status);
 }
 
-__device__ void run_epilogue(const QkvParams& p, uint8_t* smem, uint32_t tmem_base,
-                             uint32_t bar_tfull, uint32_t bar_tempty, const float* gam,
-                             volatile int* abort_flag) {
+// Position of token row m, clamped (and reported) when outside the cache.
+__device__ __forceinline__ const float* rope_row_for(const QkvParams& p, int m, bool row_valid) {
+    int64_t pos = 0;
+    if (row_valid) {
+        pos = __ldg(p.positions + m);
+        if (pos < 0 || pos >= p.rope_rows) {
+            report_status(p.status, FU_DEV_POSITION_RANGE, 0);
+            pos = 0;
+        }
+    }
+    return p.rope + pos * 128;
+}
+
+// Everything after the projection for one head row, read from TMEM lane
+// `taddr` (this thread's token row, the head's first column): optional
+// projection dump, RMSNorm + RoPE for Q/K (V as is), swizzled staging, and
+// the warp's two bulk tensor stores of its 32-row box into the destination
+// rank's receive buffer.  Pass 1 (Q/K) sums the squares of the BF16-rounded
+// projection; pass 2 re-reads TMEM sixteen lo/hi column pairs at a time, so
+// the head row never has to be held in registers next to its cos|sin.
+__device__ __forceinline__ void emit_head(const QkvParams& p, uint32_t taddr, int h, int m,
+                                          bool row_valid, int box_row0,
+                                          const float4 (&cosv)[16], const float4 (&sinv)[16],
+                                          const float* gam, uint8_t* box_lo, uint8_t* box_hi,
+                                          int lane) {
+    const uint32_t swz_row = lane * 128;
+    const int swz = lane & 7;
+    int comp, head_id, per_gpu;
+    if (h < p.q_heads) {
+        comp = 0; head_id = h; per_gpu = p.q_per_gpu;
+    } else if (h < p.q_heads + p.kv_heads) {
+        comp = 1; head_id = h - p.q_heads; per_gpu = p.kv_per_gpu;
+    } else {
+        comp = 2; head_id = h - p.q_heads - p.kv_heads; per_gpu = p.kv_per_gpu;
+    }
+    const int dst = head_id / per_gpu;
+    const int dst_col = head_id % per_gpu;
+
+    float scale = 0.f;
+    if (comp < 2) {
+        float ss = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld_32cols(taddr + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const float2 f = unpack_bf16x2(pack_bf16x2(__uint_as_float(r[2 * i]),
+                                                           __uint_as_float(r[2 * i + 1])));
+                ss = fmaf(f.x, f.x, ss);       // squares of BF16 values are exact in FP32
+                ss = fmaf(f.y, f.y, ss);
+            }
+        }
+        const float eps = comp == 0 ? p.q_eps : p.k_eps;
+        scale = __frsqrt_rn(__fadd_rn(ss * (1.0f / 128.0f), eps));
+    }
+
+    // The staging boxes must have been read by the previous store.
+    if (lane == 0) bulk_wait_read_all();
+    __syncwarp();
+
+    const float* g = gam + (comp < 2 ? comp : 0) * 128;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {               // columns 16q..16q+15 and 64+16q..
+        uint32_t lo_raw[16], hi_raw[16];
+        tmem_ld_16cols(taddr + 16 * q, lo_raw);
+        tmem_ld_16cols(taddr + 64 + 16 * q, hi_raw);
+        tmem_ld_wait();
+        uint32_t lo_p[8], hi_p[8];              // the BF16 projection (pairs of columns)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            lo_p[i] = pack_bf16x2(__uint_as_float(lo_raw[2 * i]), __uint_as_float(lo_raw[2 * i + 1]));
+            hi_p[i] = pack_bf16x2(__uint_as_float(hi_raw[2 * i]), __uint_as_float(hi_raw[2 * i + 1]));
+        }
+        if (p.gemm_out != nullptr && row_valid) {
+            __nv_bfloat16* row = p.gemm_out + static_cast<int64_t>(m) * p.N + h * 128;
+            uint4* dlo = reinterpret_cast<uint4*>(row + 16 * q);
+            uint4* dhi = reinterpret_cast<uint4*>(row + 64 + 16 * q);
+            dlo[0] = make_uint4(lo_p[0], lo_p[1], lo_p[2], lo_p[3]);
+            dlo[1] = make_uint4(lo_p[4], lo_p[5], lo_p[6], lo_p[7]);
+            dhi[0] = make_uint4(hi_p[0], hi_p[1], hi_p[2], hi_p[3]);
+            dhi[1] = make_uint4(hi_p[4], hi_p[5], hi_p[6], hi_p[7]);
+        }
+        uint32_t olo[8], ohi[8];
+        if (comp < 2) {
+            const float cs[16] = {cosv[4 * q].x, cosv[4 * q].y, cosv[4 * q].z, cosv[4 * q].w,
+                                  cosv[4 * q + 1].x, cosv[4 * q + 1].y, cosv[4 * q + 1].z,
+                                  cosv[4 * q + 1].w, cosv[4 * q + 2].x, cosv[4 * q + 2].y,
+                                  cosv[4 * q + 2].z, cosv[4 * q + 2].w, cosv[4 * q + 3].x,
+                                  cosv[4 * q + 3].y, cosv[4 * q + 3].z, cosv[4 * q + 3].w};
+            const float sn[16] = {sinv[4 * q].x, sinv[4 * q].y, sinv[4 * q].z, sinv[4 * q].w,
+                                  sinv[4 * q + 1].x, sinv[4 * q + 1].y, sinv[4 * q + 1].z,
+                                  sinv[4 * q + 1].w, sinv[4 * q + 2].x, sinv[4 * q + 2].y,
+                                  sinv[4 * q + 2].z, sinv[4 * q + 2].w, sinv[4 * q + 3].x,
+                                  sinv[4 * q + 3].y, sinv[4 * q + 3].z, sinv[4 * q + 3].w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int j = 16 * q + 2 * i;
+                const float2 lo = unpack_bf16x2(lo_p[i]);
+                const float2 hi = unpack_bf16x2(hi_p[i]);
+                // RMSNorm, * gamma, BF16 boundary (torch_base.py:56-61).
+                const float nl0 = bf16_round(__fmul_rn(__fmul_rn(lo.x, scale), g[j]));
+                const float nl1 = bf16_round(__fmul_rn(__fmul_rn(lo.y, scale), g[j + 1]));
+                const float nh0 = bf16_round(__fmul_rn(__fmul_rn(hi.x, scale), g[j + 64]));
+                const float nh1 = bf16_round(__fmul_rn(__fmul_rn(hi.y, scale), g[j + 65]));
+                // NeoX rotation, separately rounded products (torch_base.py:62-63).
+                const float c0 = cs[2 * i], c1 = cs[2 * i + 1];
+                const float s0 = sn[2 * i], s1 = sn[2 * i + 1];
+                olo[i] = pack_bf16x2(__fsub_rn(__fmul_rn(nl0, c0), __fmul_rn(nh0, s0)),
+                                     __fsub_rn(__fmul_rn(nl1, c1), __fmul_rn(nh1, s1)));
+                ohi[i] = pack_bf16x2(__fadd_rn(__fmul_rn(nh0, c0), __fmul_rn(nl0, s0)),
+                                     __fadd_rn(__fmul_rn(nh1, c1), __fmul_rn(nl1, s1)));
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                olo[i] = lo_p[i];
+                ohi[i] = hi_p[i];
+            }
+        }
+        // 16-byte chunks 2q and 2q+1 of the row in each box (128-byte swizzle).
+        const uint32_t off0 = swz_row + (((2 * q) ^ swz) << 4);
+        const uint32_t off1 = swz_row + (((2 * q + 1) ^ swz) << 4);
+        *reinterpret_cast<uint4*>(box_lo + off0) = make_uint4(olo[0], olo[1], olo[2], olo[3]);
+        *reinterpret_cast<uint4*>(box_lo + off1) = make_uint4(olo[4], olo[5], olo[6], olo[7]);
+        *reinterpret_cast<uint4*>(box_hi + off0) = make_uint4(ohi[0], ohi[1], ohi[2], ohi[3]);
+        *reinterpret_cast<uint4*>(box_hi + off1) = make_uint4(ohi[4], ohi[5], ohi[6], ohi[7]);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        // Rows past L in this source's batch are clipped by the tensor map.
+        const CUtensorMap* tm = &p.tm_out[comp * FU_MAX_SP + dst];
+        tma_store_3d(tm, smem_u32(box_lo), dst_col * 128, box_row0, p.sp_rank);
+        tma_store_3d(tm, smem_u32(box_hi), dst_col * 128 + 64, box_row0, p.sp_rank);
+        bulk_commit_group();
+    }
+}
+
+__device__ void run_epilogue(const QkvParams& p, const Sched& sc, uint8_t* smem,
+                             uint32_t tmem_base, uint32_t bar_tfull, uint32_t bar_tempty,
+                             const float* gam, volatile int* abort_flag) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int quarter = warp & 3;           // TMEM lanes this warp may access
     const int row_in_tile = quarter * 32 + lane;
     uint8_t* box_lo = smem + OFF_STG + (warp - 2) * STAGING_PER_WARP;
     uint8_t* box_hi = box_lo + BOX_BYTES;
-    const uint32_t swz_row = lane * 128;
-    const int swz = lane & 7;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
 
     int local = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
+    for (int tile = sc.first; tile < sc.end; tile += sc.stride, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         const int m_blk = tile / p.num_n_blocks;
         const int n_blk = tile % p.num_n_blocks;
+        const int m = m_blk * BM + row_in_tile;
+        const bool row_valid = m < p.L;
+        // This row's cos|sin, fetched while the tensor cores still work on the
+        // tile (shared by both heads).
+        float4 cosv[16], sinv[16];
+        {
+            const float4* rope_row =
+                reinterpret_cast<const float4*>(rope_row_for(p, m, row_valid));
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                cosv[i] = __ldg(rope_row + i);
+                sinv[i] = __ldg(rope_row + 16 + i);
+            }
+        }
         if (!fu_wait_parity(bar_tfull + 8 * acc, acc_phase, abort_flag, p.timeout_ns, p.status,
                             W_TFULL))
             break;
         tc_fence_after();
-
-        const int m = m_blk * BM + row_in_tile;
-        const bool row_valid = m < p.L;
-        int64_t pos = 0;
-        if (row_valid) {
-            pos = __ldg(p.positions + m);
-            if (pos < 0 || pos >= p.rope_rows) {
-                report_status(p.status, FU_DEV_POSITION_RANGE, 0);
-                pos = 0;
-            }
-        }
-        const float* rope_row = p.rope + pos * 128;
-
+        const int heads_here = min(2, p.heads - n_blk * 2);   // odd head count: last tile has one
 #pragma unroll 1
-        for (int hs = 0; hs < 2; ++hs) {
-            const int h = n_blk * 2 + hs;
-            if (h >= p.heads) break;        // odd head count: the last tile has one head
-
-            // TMEM -> registers, rounded to BF16 exactly as the BF16 projection output.
-            uint32_t packed[64];
-            float ss = 0.f;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t r[32];
-                tmem_ld_32cols(tmem_base + lane_addr + acc * BN + hs * 128 + c * 32, r);
-                tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const uint32_t u = pack_bf16x2(__uint_as_float(r[2 * i]),
-                                                   __uint_as_float(r[2 * i + 1]));
-                    packed[c * 16 + i] = u;
-                    const float2 f = unpack_bf16x2(u);
-                    ss = fmaf(f.x, f.x, ss);   // squares of BF16 values are exact in FP32
-                    ss = fmaf(f.y, f.y, ss);
-                }
-            }
-            if (hs == 1 || n_blk * 2 + 1 >= p.heads) {
-                // Both heads of this accumulator are in registers: hand TMEM back.
-                tc_fence_before();
-                mbar_arrive(bar_tempty + 8 * acc);
-            }
-
-            if (p.gemm_out != nullptr && row_valid) {
-                uint4* dst = reinterpret_cast<uint4*>(p.gemm_out + static_cast<int64_t>(m) * p.N +
-                                                      h * 128);
-#pragma unroll
-                for (int c = 0; c < 16; ++c)
-                    dst[c] = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
-                                        packed[4 * c + 3]);
-            }
-
-            int comp, head_id, per_gpu;
-            if (h < p.q_heads) {
-                comp = 0; head_id = h; per_gpu = p.q_per_gpu;
-            } else if (h < p.q_heads + p.kv_heads) {
-                comp = 1; head_id = h - p.q_heads; per_gpu = p.kv_per_gpu;
-            } else {
-                comp = 2; head_id = h - p.q_heads - p.kv_heads; per_gpu = p.kv_per_gpu;
-            }
-            const int dst = head_id / per_gpu;
-            const int dst_col = head_id % per_gpu;
-
-            // The staging boxes must have been read by the previous store.
-            if (lane == 0) bulk_wait_read_all();
-            __syncwarp();
-
-            if (comp < 2) {
-                const float eps = comp == 0 ? p.q_eps : p.k_eps;
-                const float* g = gam + comp * 128;
-                const float mean = ss * (1.0f / 128.0f);
-                const float scale = __frsqrt_rn(__fadd_rn(mean, eps));
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const float4 c0 = __ldg(reinterpret_cast<const float4*>(rope_row + 8 * c));
-                    const float4 c1 = __ldg(reinterpret_cast<const float4*>(rope_row + 8 * c + 4));
-                    const float4 s0 = __ldg(reinterpret_cast<const float4*>(rope_row + 64 + 8 * c));
-                    const float4 s1 =
-                        __ldg(reinterpret_cast<const float4*>(rope_row + 64 + 8 * c + 4));
-                    const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-                    const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-                    uint32_t olo[4], ohi[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int j = 8 * c + 2 * i;
-                        const float2 lo = unpack_bf16x2(packed[4 * c + i]);
-                        const float2 hi = unpack_bf16x2(packed[32 + 4 * c + i]);
-                        // RMSNorm, * gamma, BF16 boundary (torch_base.py:56-61).
-                        const float nl0 = bf16_round(__fmul_rn(__fmul_rn(lo.x, scale), g[j]));
-                        const float nl1 = bf16_round(__fmul_rn(__fmul_rn(lo.y, scale), g[j + 1]));
-                        const float nh0 = bf16_round(__fmul_rn(__fmul_rn(hi.x, scale), g[j + 64]));
-                        const float nh1 = bf16_round(__fmul_rn(__fmul_rn(hi.y, scale), g[j + 65]));
-                        // NeoX rotation, separately rounded products (torch_base.py:62-63).
-                        const float r0 = __fsub_rn(__fmul_rn(nl0, cs[2 * i]), __fmul_rn(nh0, sn[2 * i]));
-                        const float r1 =
-                            __fsub_rn(__fmul_rn(nl1, cs[2 * i + 1]), __fmul_rn(nh1, sn[2 * i + 1]));
-                        const float t0 = __fadd_rn(__fmul_rn(nh0, cs[2 * i]), __fmul_rn(nl0, sn[2 * i]));
-                        const float t1 =
-                            __fadd_rn(__fmul_rn(nh1, cs[2 * i + 1]), __fmul_rn(nl1, sn[2 * i + 1]));
-                        olo[i] = pack_bf16x2(r0, r1);
-                        ohi[i] = pack_bf16x2(t0, t1);
-                    }
-                    const uint32_t off = swz_row + ((c ^ swz) << 4);
-                    *reinterpret_cast<uint4*>(box_lo + off) = make_uint4(olo[0], olo[1], olo[2], olo[3]);
-                    *reinterpret_cast<uint4*>(box_hi + off) = make_uint4(ohi[0], ohi[1], ohi[2], ohi[3]);
-                }
-            } else {
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const uint32_t off = swz_row + ((c ^ swz) << 4);
-                    *reinterpret_cast<uint4*>(box_lo + off) = make_uint4(
-                        packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
-                    *reinterpret_cast<uint4*>(box_hi + off) =
-                        make_uint4(packed[32 + 4 * c], packed[33 + 4 * c], packed[34 + 4 * c],
-                                   packed[35 + 4 * c]);
-                }
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                // Rows past L in this source's batch are clipped by the tensor map.
-                const CUtensorMap* tm = &p.tm_out[comp * FU_MAX_SP + dst];
-                const int row0 = m_blk * BM + quarter * 32;
-                tma_store_3d(tm, smem_u32(box_lo), dst_col * 128, row0, p.sp_rank);
-                tma_store_3d(tm, smem_u32(box_hi), dst_col * 128 + 64, row0, p.sp_rank);
-                bulk_commit_group();
-            }
-        }
+        for (int hs = 0; hs < heads_here; ++hs)
+            emit_head(p, tmem_base + lane_addr + acc * BN + hs * 128, n_blk * 2 + hs, m,
+                      row_valid, m_blk * BM + quarter * 32, cosv, sinv, gam, box_lo, box_hi,
+                      lane);
+        // Both heads of this accumulator have been read: hand TMEM back.
+        tc_fence_before();
+        mbar_arrive(bar_tempty + 8 * acc);
     }
     if (lane == 0) {
         bulk_wait_all();                    // peer writes performed
         fence_proxy_async_global();
     }
     __syncwarp();
+}
+
+// Split mode, step 1 (epilogue warps): park this CTA's FP32 partial
+// accumulator of the tile in its own shared memory (the operand ring, idle by
+// now), rows of PART_STRIDE bytes.  Only warps holding valid rows copy.
+__device__ void run_split_partial(const QkvParams& p, const Sched& sc, uint8_t* smem,
+                                  uint32_t tmem_base, uint32_t bar_tfull,
+                                  volatile int* abort_flag) {
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int quarter = warp & 3;
+    const int m_blk = sc.first / p.num_n_blocks;
+    if (!fu_wait_parity(bar_tfull, 0, abort_flag, p.timeout_ns, p.status, W_TFULL)) return;
+    tc_fence_after();
+    if (m_blk * BM + quarter * 32 >= p.L) return;          // no valid row in this warp
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    float* row = reinterpret_cast<float*>(smem + OFF_A + (quarter * 32 + lane) * PART_STRIDE);
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32cols(tmem_base + lane_addr + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            reinterpret_cast<float4*>(row + c * 32)[i] =
+                make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                            __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+    }
+}
+
+// Split mode, step 2 (epilogue warps of every cluster CTA, after a cluster
+// barrier): one item = one valid token row x one head.  A warp takes two items
+// at a time; lane l owns columns 4l..4l+3 of the head, loads the partials of
+// every cluster CTA at once (coalesced distributed-shared-memory reads) and
+// sums them in rank order (deterministic).  The RMSNorm sum is a warp
+// reduction, the NeoX partner of lane l is lane l^16, and the row leaves as
+// one coalesced 256-byte store into the destination rank's receive buffer.
+__device__ __forceinline__ void split_item_load(const QkvParams& p, uint32_t local, int splits,
+                                                float4& t) {
+    float4 v[FU_MAX_SP];
+#pragma unroll
+    for (int s = 0; s < FU_MAX_SP; ++s)
+        if (s < splits) v[s] = ld_cluster_f32x4(map_cluster_smem(local, s));
+    t = v[0];
+#pragma unroll
+    for (int s = 1; s < FU_MAX_SP; ++s)
+        if (s < splits) {
+            t.x += v[s].x; t.y += v[s].y; t.z += v[s].z; t.w += v[s].w;
+        }
+}
+
+__device__ __forceinline__ void split_item_emit(const QkvParams& p, const float4& acc, int m,
+                                                int h, const float* gam, int lane) {
+    // BF16 projection of columns 4l..4l+3 of head h, token row m.
+    const uint32_t u0 = pack_bf16x2(acc.x, acc.y);
+    const uint32_t u1 = pack_bf16x2(acc.z, acc.w);
+    float v[4];
+    {
+        const float2 a = unpack_bf16x2(u0), b = unpack_bf16x2(u1);
+        v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    }
+    if (p.gemm_out != nullptr)
+        *reinterpret_cast<uint2*>(p.gemm_out + static_cast<int64_t>(m) * p.N + h * 128 + 4 * lane) =
+            make_uint2(u0, u1);
+    int comp, head_id, per_gpu;
+    if (h < p.q_heads) {
+        comp = 0; head_id = h; per_gpu = p.q_per_gpu;
+    } else if (h < p.q_heads + p.kv_heads) {
+        comp = 1; head_id = h - p.q_heads; per_gpu = p.kv_per_gpu;
+    } else {
+        comp = 2; head_id = h - p.q_heads - p.kv_heads; per_gpu = p.kv_per_gpu;
+    }
+    const int dst = head_id / per_gpu;
+    const int dst_col = head_id % per_gpu;
+    uint2 out = make_uint2(u0, u1);
+    if (comp < 2) {
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ss = fmaf(v[i], v[i], ss);
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float eps = comp == 0 ? p.q_eps : p.k_eps;
+        const float scale = __frsqrt_rn(__fadd_rn(ss * (1.0f / 128.0f), eps));
+        const float* g = gam + comp * 128 + 4 * lane;
+        float n[4], partner[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) n[i] = bf16_round(__fmul_rn(__fmul_rn(v[i], scale), g[i]));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, n[i], 16);
+        int64_t pos = __ldg(p.positions + m);
+        if (pos < 0 || pos >= p.rope_rows) {
+            report_status(p.status, FU_DEV_POSITION_RANGE, 0);
+            pos = 0;
+        }
+        const int j0 = 4 * (lane & 15);
+        const float4 cs = __ldg(reinterpret_cast<const float4*>(p.rope + pos * 128 + j0));
+        const float4 sn = __ldg(reinterpret_cast<const float4*>(p.rope + pos * 128 + 64 + j0));
+        const float c4[4] = {cs.x, cs.y, cs.z, cs.w};
+        const float s4[4] = {sn.x, sn.y, sn.z, sn.w};
+        float r[4];
+        if (lane < 16) {        // lo half: lo*cos - hi*sin
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                r[i] = __fsub_rn(__fmul_rn(n[i], c4[i]), __fmul_rn(partner[i], s4[i]));
+        } else {                // hi half: hi*cos + lo*sin
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                r[i] = __fadd_rn(__fmul_rn(n[i], c4[i]), __fmul_rn(partner[i], s4[i]));
+        }
+        out = make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
+    }
+    const int64_t cols = static_cast<int64_t>(per_gpu) * 128;
+    __nv_bfloat16* base = static_cast<__nv_bfloat16*>(p.out_base[comp * FU_MAX_SP + dst]);
+    *reinterpret_cast<uint2*>(base + (static_cast<int64_t>(p.sp_rank) * p.L + m) * cols +
+                              dst_col * 128 + 4 * lane) = out;
+}
+
+__device__ void run_split_reduce(const QkvParams& p, const Sched& sc, uint8_t* smem,
+                                 const float* gam) {
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int m_blk = sc.first / p.num_n_blocks;
+    const int n_blk = sc.first % p.num_n_blocks;
+    const int rows = min(BM, p.L - m_blk * BM);
+    const int heads_here = min(2, p.heads - n_blk * 2);
+    const int items = rows * heads_here;
+    const int workers = 4 * p.splits;
+    const uint32_t part = smem_u32(smem + OFF_A);
+    // Item i: row i / heads_here, head slot i % heads_here.
+    for (int i0 = (warp - 2) * p.splits + sc.split; i0 < items; i0 += 2 * workers) {
+        const int i1 = i0 + workers;
+        const bool has1 = i1 < items;
+        const int r0 = i0 / heads_here, hs0 = i0 % heads_here;
+        const int r1 = has1 ? i1 / heads_here : r0, hs1 = has1 ? i1 % heads_here : hs0;
+        float4 a0, a1;
+        split_item_load(p, part + r0 * PART_STRIDE + (hs0 * 128 + 4 * lane) * 4, p.splits, a0);
+        split_item_load(p, part + r1 * PART_STRIDE + (hs1 * 128 + 4 * lane) * 4, p.splits, a1);
+        split_item_emit(p, a0, m_blk * BM + r0, n_blk * 2 + hs0, gam, lane);
+        if (has1) split_item_emit(p, a1, m_blk * BM + r1, n_blk * 2 + hs1, gam, lane);
+    }
 }
 
 // ------------------------------------------------------------ kernel
@@ -380,6 +589,8 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const Sched sc = make_sched(p);
+    const bool split_mode = p.splits > 1;
 
     const uint32_t bar_base = smem_u32(smem + OFF_BAR);
     const uint32_t bar_full = bar_base;
@@ -418,15 +629,17 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
     const uint32_t tmem_base = *tmem_holder;
 
     if (warp == 0) {
-        if (lane == 0) run_producer(p, smem, bar_full, bar_empty, abort_flag);
+        if (lane == 0) run_producer(p, sc, smem, bar_full, bar_empty, abort_flag);
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0)
-            run_mma(p, smem, tmem_base, bar_full, bar_empty, bar_tfull, bar_tempty, bar_mma_done,
-                    abort_flag);
+            run_mma(p, sc, smem, tmem_base, bar_full, bar_empty, bar_tfull, bar_tempty,
+                    bar_mma_done, abort_flag);
         __syncwarp();
+    } else if (split_mode) {
+        run_split_partial(p, sc, smem, tmem_base, bar_tfull, abort_flag);
     } else {
-        run_epilogue(p, smem, tmem_base, bar_tfull, bar_tempty, gam, abort_flag);
+        run_epilogue(p, sc, smem, tmem_base, bar_tfull, bar_tempty, gam, abort_flag);
     }
 
     tc_fence_before();
@@ -434,30 +647,47 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
 
+    if (split_mode) {
+        // Every CTA of the cluster reaches both barriers on every path, so a
+        // CTA that gave up on a wait cannot strand its peers here.
+        cluster_sync_all();                 // partials visible cluster-wide
+        if (warp >= 2) run_split_reduce(p, sc, smem, gam);
+        cluster_sync_all();                 // peers are done reading this CTA's partial
+    }
+
     // ---- exit barrier: the last CTA of this rank joins the SP group.
+    // Every CTA's output is complete (stores waited for, then the barriers
+    // above).  A world of one needs only GPU scope; with peers, one
+    // system-scope fence per CTA makes its remote stores visible beyond this
+    // GPU before it is counted, and the last CTA's release stores publish the
+    // epoch (cumulative over every counted CTA).
     if (threadIdx.x == 64) {
         const bool aborted = *abort_flag != 0;
         uint32_t* my_sync = p.sync[p.sp_rank];
-        fence_acq_rel_sys();
+        if (p.sp_size > 1) fence_acq_rel_sys(); else fence_acq_rel_gpu();
         const uint32_t old =
             atom_add_acq_rel_gpu_u32(my_sync + FU_SYNC_COUNTER, aborted ? 0x10001u : 1u);
         if ((old & 0xFFFFu) == gridDim.x - 1) {
             const bool any_abort = aborted || (old >> 16) != 0;
             *reinterpret_cast<volatile uint32_t*>(my_sync + FU_SYNC_COUNTER) = 0u;
             if (!any_abort) {
-                fence_acq_rel_sys();
-                for (int d = 0; d < p.sp_size; ++d) st_release_sys_u32(p.sync[d] + p.sp_rank, p.epoch);
-                if (p.wait_peers) {
-                    const uint64_t t0 = globaltimer_ns();
-                    for (int s = 0; s < p.sp_size; ++s) {
-                        while (static_cast<int32_t>(ld_acquire_sys_u32(my_sync + s) - p.epoch) < 0) {
-                            if (globaltimer_ns() - t0 > p.timeout_ns) {
-                                report_status(p.status, FU_DEV_PEER_TIMEOUT, s);
-                                break;
+                if (p.sp_size == 1) {
+                    st_release_gpu_u32(my_sync, p.epoch);
+                } else {
+                    for (int d = 0; d < p.sp_size; ++d)
+                        st_release_sys_u32(p.sync[d] + p.sp_rank, p.epoch);
+                    if (p.wait_peers) {
+                        const uint64_t t0 = globaltimer_ns();
+                        for (int s = 0; s < p.sp_size; ++s) {
+                            while (static_cast<int32_t>(ld_acquire_sys_u32(my_sync + s) - p.epoch) <
+                                   0) {
+                                if (globaltimer_ns() - t0 > p.timeout_ns) {
+                                    report_status(p.status, FU_DEV_PEER_TIMEOUT, s);
+                                    break;
+                                }
                             }
                         }
                     }
-                    fence_acq_rel_sys();
                 }
             }
         }
@@ -506,6 +736,7 @@ static int encode(CUtensorMap* map, const void* base, int rank, const cuuint64_t
 struct fu_qkv_ctx {
     fu_qkv_topology topo;
     int sm_count = 0;
+    int max_clusters[9] = {0};    // co-resident clusters of each size (index = CTAs per cluster)
     uint32_t epoch = 0;
     int last_grid = 0;
     // Tensor-map caches.
@@ -517,6 +748,36 @@ struct fu_qkv_ctx {
 };
 
 using namespace fu;
+
+// Split-K factor for `tiles` tiles of `kb` k-blocks with `rows` valid token
+// rows per tile: 1 (persistent grid) unless a cluster split is estimated to be
+// faster.  The estimates (microseconds) were fitted on B200 at H=4096:
+//   persistent  12 + ceil(tiles / SMs) * 0.40 * kb
+//   split s      8 + waves * (0.55 * ceil(kb / s) + 2.5 * ceil(2 rows / 8 s))
+// (a split's CTAs share HBM bandwidth, and its reduction walks rows x 2 heads
+// items two per warp over the cluster's 4 s epilogue warps).  `forced` (from
+// FU_FWD_SPLITS in the call's flags) overrides the choice when the device can
+// co-schedule clusters of that size.
+static int choose_splits(const fu_qkv_ctx* ctx, int64_t tiles, int kb, int64_t rows, int forced) {
+    if (forced >= 1 && forced <= 8)
+        return forced <= kb && (forced == 1 || ctx->max_clusters[forced] > 0) ? forced : 1;
+    const int64_t sms = ctx->sm_count;
+    double best_cost = 12.0 + static_cast<double>((tiles + sms - 1) / sms) * 0.40 * kb;
+    int best = 1;
+    for (int s = 2; s <= 8 && s <= kb; ++s) {
+        const int64_t cap = ctx->max_clusters[s];
+        if (cap <= 0) continue;
+        const int64_t waves = (tiles + cap - 1) / cap;
+        const int64_t iters = (2 * rows + 8 * s - 1) / (8 * s);
+        const double cost = 8.0 + static_cast<double>(waves) *
+                                      (0.55 * ((kb + s - 1) / s) + 2.5 * static_cast<double>(iters));
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = s;
+        }
+    }
+    return best;
+}
 
 extern "C" int fu_qkv_create(const fu_qkv_topology* topo, fu_qkv_ctx** out) {
     if (topo == nullptr || out == nullptr) return set_error(FU_ERR_INVALID, "null argument");
@@ -560,6 +821,27 @@ extern "C" int fu_qkv_create(const fu_qkv_topology* topo, fu_qkv_ctx** out) {
     if (e != cudaSuccess)
         return set_error(FU_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     auto* ctx = new fu_qkv_ctx();
+    cudaSetDevice(topo->device);
+    for (int cs = 2; cs <= 8; ++cs) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(cs * 16, 1, 1);
+        cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+        cfg.dynamicSmemBytes = SMEM_ALLOC;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = cs;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, fused_qkv_exchange_kernel, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        ctx->max_clusters[cs] = n;
+    }
+    cudaSetDevice(prev);
     ctx->topo = *topo;
     if (ctx->topo.timeout_ns == 0) ctx->topo.timeout_ns = 5000000000ull;
     ctx->sm_count = sms;
@@ -646,7 +928,12 @@ extern "C" int fu_qkv_forward(fu_qkv_ctx* ctx, const void* x, const void* w,
     p.k_gamma = k_gamma;
     p.rope = rope;
     p.gemm_out = static_cast<__nv_bfloat16*>(gemm_out);
-    for (int d = 0; d < FU_MAX_SP; ++d) p.sync[d] = d < S ? t.sync[d] : nullptr;
+    for (int d = 0; d < FU_MAX_SP; ++d) {
+        p.sync[d] = d < S ? t.sync[d] : nullptr;
+        p.out_base[0 * FU_MAX_SP + d] = d < S ? t.q_recv[d] : nullptr;
+        p.out_base[1 * FU_MAX_SP + d] = d < S ? t.k_recv[d] : nullptr;
+        p.out_base[2 * FU_MAX_SP + d] = d < S ? t.v_recv[d] : nullptr;
+    }
     p.status = t.status;
     p.timeout_ns = t.timeout_ns;
     p.L = static_cast<int32_t>(L);
@@ -672,14 +959,34 @@ extern "C" int fu_qkv_forward(fu_qkv_ctx* ctx, const void* x, const void* w,
     if (p.epoch == 0) p.epoch = ++ctx->epoch;   // 0 is the flags' initial value
     p.wait_peers = (flags & FU_FWD_NO_PEER_WAIT) ? 0u : 1u;
 
-    const int grid = static_cast<int>(tiles < ctx->sm_count ? tiles : ctx->sm_count);
+    p.splits = choose_splits(ctx, tiles, p.k_blocks, L < BM ? L : BM,
+                             static_cast<int>((flags >> 8) & 0xFu));
+    const int grid = p.splits > 1 ? static_cast<int>(tiles) * p.splits
+                                  : static_cast<int>(tiles < ctx->sm_count ? tiles : ctx->sm_count);
     ctx->last_grid = grid;
     int prev = 0;
     cudaGetDevice(&prev);
     if (prev != t.device) cudaSetDevice(t.device);
-    fused_qkv_exchange_kernel<<<grid, NUM_THREADS, SMEM_ALLOC,
-                                static_cast<cudaStream_t>(stream)>>>(p);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e;
+    if (p.splits > 1) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid, 1, 1);
+        cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+        cfg.dynamicSmemBytes = SMEM_ALLOC;
+        cfg.stream = static_cast<cudaStream_t>(stream);
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = p.splits;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, fused_qkv_exchange_kernel, p);
+    } else {
+        fused_qkv_exchange_kernel<<<grid, NUM_THREADS, SMEM_ALLOC,
+                                    static_cast<cudaStream_t>(stream)>>>(p);
+        e = cudaGetLastError();
+    }
     if (prev != t.device) cudaSetDevice(prev);
     if (e != cudaSuccess) return set_error(FU_ERR_CUDA, "launch failed: %s", cudaGetErrorString(e));
     return FU_OK;

@@ -67,6 +67,10 @@ enum fu_device_status {
 
 /* Flags for fu_qkv_forward. */
 #define FU_FWD_NO_PEER_WAIT 1u  /* signal peers but do not wait for them */
+/* Split-K factor 1..8 (0 = choose automatically): with n > 1 each tile is
+ * reduced by a cluster of n CTAs that sum their partials over distributed
+ * shared memory; 1 forces the persistent one-CTA-per-tile grid. */
+#define FU_FWD_SPLITS(n) (((uint32_t)(n) & 0xFu) << 8)
 
 FU_API const char* fu_last_error(void);
 FU_API int fu_version(void);

@@ -38,9 +38,9 @@ def oracle_topology(cfg):
                            cfg.hidden_size)
 
 
-def run_group(cfg, tokens, tp_rank=0, seed=0):
+def run_group(cfg, tokens, tp_rank=0, seed=0, splits=0):
     """Emulate SP group ``tp_rank`` of ``cfg`` on one GPU; return everything the
-    checks need."""
+    checks need.  ``splits`` forces the split-K factor (0: automatic)."""
     topo = oracle_topology(cfg)
     xs, pos, params = make_world(cfg, tokens, seed=seed)
     S = cfg.sp_size
@@ -54,10 +54,14 @@ def run_group(cfg, tokens, tp_rank=0, seed=0):
         gparams = [to_device(params[r], dev) for r in ranks]
         dumps = [torch.empty(tokens, topo.packed_width, dtype=torch.bfloat16, device=dev)
                  for _ in ranks]
-        group.run(gx, gp, gparams, gemm_outs=dumps)
+        group.run(gx, gp, gparams, gemm_outs=dumps,
+                  flags=_C.FU_FWD_NO_PEER_WAIT | _C.FU_FWD_SPLITS(splits))
         torch.cuda.synchronize()
         assert group.status.value == 0, _C.decode_status(group.status.value)
         assert group.flags_ok()
+        if splits > 1:
+            tiles = -(-tokens // 128) * -(-(topo.local_q_heads + 2 * topo.local_kv_heads) // 2)
+            assert group.ops[0].last_grid == tiles * splits
         got = [tuple(t.cpu() for t in o) for o in group.outputs(tokens)]
         full = [tuple(b.cpu() for b in bufs) for bufs in group.recv]
         dumps = [d.cpu() for d in dumps]
@@ -143,6 +147,25 @@ def test_emulated_sp_group(cfg_name, tokens, tp_rank):
     check_group(run_group(CONFIGS[cfg_name], tokens, tp_rank=tp_rank))
 
 
+@pytest.mark.parametrize("tokens,splits", [
+    (1, 2), (1, 3), (1, 4), (1, 6), (1, 8), (65, 4), (129, 3), (300, 2), (300, 5), (128, 1),
+])
+def test_split_k_cluster_reduction(tokens, splits):
+    """Split-K over a cluster (partials summed over distributed shared memory)
+    at every factor, including factors that do not divide the k-blocks."""
+    base = CONFIGS["c1"]
+    cfg = base.__class__("c1_p1", 1, 1, base.hidden_size, base.num_heads, base.num_kv_heads,
+                         base.tokens, base.max_position)
+    check_group(run_group(cfg, tokens, splits=splits))
+
+
+@pytest.mark.parametrize("cfg_name,tokens,tp_rank,splits", [
+    ("c3", 1, 1, 8), ("c3", 129, 0, 4), ("c1", 64, 0, 2), ("c0", 64, 0, 3),
+])
+def test_split_k_emulated_groups(cfg_name, tokens, tp_rank, splits):
+    check_group(run_group(CONFIGS[cfg_name], tokens, tp_rank=tp_rank, splits=splits))
+
+
 def exact_world(S, H, q_heads, kv_heads, tokens, seed=0):
     """Inputs on which every step is exact in any order, so the kernel must
     match the oracle bit for bit: one-hot hidden rows select weight rows whose
@@ -172,11 +195,11 @@ def exact_world(S, H, q_heads, kv_heads, tokens, seed=0):
     return xs, pos, [params] * S
 
 
-@pytest.mark.parametrize("S,H,q,kv,tokens", [
-    (1, 256, 4, 2, 65), (2, 256, 4, 2, 65), (4, 512, 8, 4, 130), (2, 128, 2, 2, 1),
-    (1, 64, 1, 1, 200),
+@pytest.mark.parametrize("S,H,q,kv,tokens,splits", [
+    (1, 256, 4, 2, 65, 1), (2, 256, 4, 2, 65, 1), (4, 512, 8, 4, 130, 1), (2, 128, 2, 2, 1, 1),
+    (1, 64, 1, 1, 200, 1), (2, 256, 4, 2, 65, 4), (4, 512, 8, 4, 130, 3), (1, 512, 4, 2, 1, 8),
 ])
-def test_bit_exact_on_exact_inputs(S, H, q, kv, tokens):
+def test_bit_exact_on_exact_inputs(S, H, q, kv, tokens, splits):
     """Placement, padding, norm, RoPE and clipping, bit for bit."""
     xs, pos, params = exact_world(S, H, q, kv, tokens)
     topo = oracle.Topology(S, S, q, kv, H)
@@ -186,7 +209,8 @@ def test_bit_exact_on_exact_inputs(S, H, q, kv, tokens):
                           max_local_tokens=tokens + 3)
     try:
         group.run([x.to(dev) for x in xs], [p.to(dev) for p in pos],
-                  [to_device(p, dev) for p in params])
+                  [to_device(p, dev) for p in params],
+                  flags=_C.FU_FWD_NO_PEER_WAIT | _C.FU_FWD_SPLITS(splits))
         torch.cuda.synchronize()
         assert group.status.value == 0
         assert group.flags_ok()

@@ -24,11 +24,13 @@ H, QH, KVH = 4096, 32, 8
 
 
 def existing_entry_point(x, pos, params, tokens):
-    """Outputs of the context-based entry point (fu_qkv_forward), world of one."""
+    """Outputs of the context-based entry point (fu_qkv_forward), world of one,
+    on the same kernel variant (one CTA per tile over the full reduction) that
+    the allocation-free entry point runs."""
     group = EmulatedGroup(sp_size=1, hidden_size=H, q_heads=QH, kv_heads=KVH,
                           max_local_tokens=tokens)
     try:
-        group.run([x], [pos], [params], flags=0)
+        group.run([x], [pos], [params], flags=_C.FU_FWD_SPLITS(1))
         torch.cuda.synchronize()
         assert group.status.value == 0
         return tuple(t.clone() for t in group.outputs(tokens)[0])
