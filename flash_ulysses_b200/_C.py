@@ -23,6 +23,11 @@ FU_SYNC_COUNTER = 32
 FU_FWD_NO_PEER_WAIT = 1
 
 
+FU_FWD_SINGLE = 1 << 12
+FU_FWD_PAIR = 2 << 12
+FU_FWD_NO_RETILE = 1 << 14
+
+
 def FU_FWD_SPLITS(n):
     """Flag bits forcing the split-K factor (0 = automatic)."""
     return (n & 0xF) << 8

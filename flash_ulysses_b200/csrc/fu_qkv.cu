@@ -39,27 +39,39 @@
 
 namespace fu {
 
-constexpr int BM = 128;                 // token rows per tile = TMEM lanes
+constexpr int BM = 128;                 // token rows per CTA tile = TMEM lanes
 constexpr int BN = 256;                 // packed columns per tile = 2 heads
 constexpr int BK = 64;                  // reduction step: one 128-byte swizzle row
-constexpr int STAGES = 4;               // shared-memory pipeline depth
 constexpr int UMMA_K = 16;              // K of one tcgen05.mma kind::f16
 constexpr int NUM_THREADS = 192;
 constexpr int NUM_EPI_THREADS = 128;
 constexpr int A_STAGE_BYTES = BM * BK * 2;                    // 16 KiB
 constexpr int B_CHUNK_BYTES = BK * 64 * 2;                    // 8 KiB: 64 columns x BK rows
-constexpr int B_STAGE_BYTES = BK * BN * 2;                    // 32 KiB
-constexpr uint32_t STAGE_TX = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int BOX_BYTES = 32 * 128;                           // 32 rows x 64 BF16
 constexpr int STAGING_PER_WARP = 2 * BOX_BYTES;               // lo and hi halves of one head
 constexpr uint32_t TMEM_COLS = 512;
 
+// Operand ring of a kernel variant.  One CTA per tile (kPair false): 4
+// stages of X [128 x 64] + W [64 x 256].  CTA pair (kPair true): each CTA
+// holds X [128 x 64] + its half of W, [64 x 128], so 6 stages fit.
+template <bool kPair>
+struct Ring {
+    static constexpr int STAGES = kPair ? 6 : 4;
+    static constexpr int B_CHUNKS = kPair ? 2 : 4;            // 64-column W boxes per CTA
+    static constexpr int B_STAGE_BYTES = B_CHUNKS * B_CHUNK_BYTES;
+    static constexpr uint32_t CTA_TX = A_STAGE_BYTES + B_STAGE_BYTES;
+    static constexpr uint32_t STAGE_TX = kPair ? 2 * CTA_TX : CTA_TX;   // the leader counts both
+    static constexpr int OFF_B = STAGES * A_STAGE_BYTES;
+    static constexpr int BYTES = OFF_B + STAGES * B_STAGE_BYTES;
+};
+static_assert(Ring<true>::BYTES == Ring<false>::BYTES, "both variants share one layout");
+
 constexpr int OFF_A = 0;
-constexpr int OFF_B = OFF_A + STAGES * A_STAGE_BYTES;
-constexpr int OFF_STG = OFF_B + STAGES * B_STAGE_BYTES;
+constexpr int OFF_STG = Ring<false>::BYTES;
 constexpr int OFF_BAR = OFF_STG + 4 * STAGING_PER_WARP;
-constexpr int NUM_BARS = 2 * STAGES + 2 + 2 + 1;
-constexpr int OFF_MISC = OFF_BAR + 128;
+constexpr int MAX_STAGES = 6;
+constexpr int NUM_BARS = 2 * MAX_STAGES + 2 + 2 + 1;
+constexpr int OFF_MISC = OFF_BAR + 256;
 constexpr int OFF_GAMMA = OFF_MISC + 64;
 constexpr int SMEM_BYTES = OFF_GAMMA + 2 * 128 * 4;
 // Split mode parks a 128 x 256 FP32 partial in the operand ring; rows are
@@ -67,7 +79,7 @@ constexpr int SMEM_BYTES = OFF_GAMMA + 2 * 128 * 4;
 constexpr int PART_STRIDE = BN * 4 + 16;
 static_assert(BM * PART_STRIDE <= OFF_STG, "split partial must fit in the operand ring");
 constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;                 // room to align the base to 1 KiB
-static_assert(NUM_BARS * 8 <= 128, "barrier area");
+static_assert(NUM_BARS * 8 <= 256, "barrier area");
 static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KiB per-CTA shared memory limit");
 
 // Where a wait gave up (second byte of the status word).
@@ -94,6 +106,9 @@ struct __align__(64) QkvParams {
     uint32_t wait_peers;
     int32_t splits;                         // >1: split-K over a cluster of this many CTAs
     void* out_base[3 * FU_MAX_SP];          // receive buffers (split mode stores rows directly)
+    int32_t num_units;                      // work units of the persistent grid
+    int32_t full_units;                     // units [0, full_units) are whole tiles; each later
+                                            // pair of units is one tile's two heads
 };
 static_assert(sizeof(QkvParams) <= 4096, "kernel parameter block too large");
 
@@ -126,17 +141,32 @@ __device__ __forceinline__ bool drain_wait(uint32_t bar, uint32_t parity, uint64
 }
 
 // ------------------------------------------------------------ schedule
-// Which tiles and which k-blocks this CTA owns.  Persistent mode (splits 1):
-// tiles blockIdx.x, +gridDim.x, ... over the full reduction.  Split mode:
-// the CTAs of one cluster share one tile; cluster rank s reduces k-blocks
-// [s*KB/S, (s+1)*KB/S).
+// Which tiles and which k-blocks this CTA owns.
+//   one CTA per tile, persistent (splits 1): tiles blockIdx.x, +gridDim.x, ...
+//   over the full reduction; a tile is 128 rows x 256 columns;
+//   split mode: the CTAs of one cluster share one tile; cluster rank s reduces
+//   k-blocks [s*KB/S, (s+1)*KB/S);
+//   CTA pairs, persistent: pair tiles of 256 rows x 256 columns over the
+//   clusters; CTA rank r of the pair owns rows [128 r, 128 r + 128).
 struct Sched {
-    int first, end, stride, kb0, kb1, split;
+    int first, end, stride, kb0, kb1, split, rank, rows_per_tile;
 };
 
+template <bool kPair>
 __device__ __forceinline__ Sched make_sched(const QkvParams& p) {
     Sched s;
-    if (p.splits > 1) {
+    s.rank = 0;
+    s.rows_per_tile = BM;
+    if (kPair) {
+        s.rank = static_cast<int>(cluster_ctarank());
+        s.rows_per_tile = 2 * BM;
+        s.split = 0;
+        s.first = static_cast<int>(blockIdx.x) / 2;
+        s.end = p.num_units;
+        s.stride = static_cast<int>(gridDim.x) / 2;
+        s.kb0 = 0;
+        s.kb1 = p.k_blocks;
+    } else if (p.splits > 1) {
         s.split = static_cast<int>(blockIdx.x) % p.splits;
         s.first = static_cast<int>(blockIdx.x) / p.splits;
         s.end = s.first + 1;
@@ -154,55 +184,118 @@ __device__ __forceinline__ Sched make_sched(const QkvParams& p) {
     return s;
 }
 
+// A work unit of the persistent grid: a whole tile (both heads, half = -1),
+// or one head of a tile (half = 0 or 1).  The last, partial round of a pair
+// grid is re-tiled into one-head units so that it takes half as long.
+struct Unit {
+    int m_blk, n_blk, half;
+};
+
+__device__ __forceinline__ Unit decode_unit(const QkvParams& p, int u) {
+    Unit un;
+    if (u < p.full_units) {
+        un.m_blk = u / p.num_n_blocks;
+        un.n_blk = u % p.num_n_blocks;
+        un.half = -1;
+    } else {
+        const int j = u - p.full_units;
+        const int t = p.full_units + (j >> 1);
+        un.m_blk = t / p.num_n_blocks;
+        un.n_blk = t % p.num_n_blocks;
+        un.half = j & 1;
+    }
+    return un;
+}
+
+// Shared-memory barrier layout (fixed offsets, up to MAX_STAGES stages).
+struct Bars {
+    uint32_t full, empty, tfull, tempty, mma_done;
+    __device__ Bars(uint32_t base)
+        : full(base), empty(base + 8 * MAX_STAGES), tfull(base + 16 * MAX_STAGES),
+          tempty(base + 16 * MAX_STAGES + 16), mma_done(base + 16 * MAX_STAGES + 32) {}
+};
+
 // ------------------------------------------------------------ roles
-__device__ void run_producer(const QkvParams& p, const Sched& sc, uint8_t* smem,
-                             uint32_t bar_full, uint32_t bar_empty, volatile int* abort_flag) {
+template <bool kPair>
+__device__ void run_producer(const QkvParams& p, const Sched& sc, uint8_t* smem, const Bars& b,
+                             volatile int* abort_flag) {
+    using R = Ring<kPair>;
     int stage = 0;
     uint32_t phase = 0;
     uint32_t issued_mask = 0;               // stages loaded at least once
     uint32_t last_parity = 0;               // per-stage parity of the last load
     const uint32_t a0 = smem_u32(smem + OFF_A);
-    const uint32_t b0 = smem_u32(smem + OFF_B);
+    const uint32_t b0 = smem_u32(smem + R::OFF_B);
     bool ok = true;
     for (int tile = sc.first; ok && tile < sc.end; tile += sc.stride) {
-        const int m_blk = tile / p.num_n_blocks;
-        const int n_blk = tile % p.num_n_blocks;
+        const Unit un = decode_unit(p, tile);
+        const int row0 = un.m_blk * sc.rows_per_tile + sc.rank * BM;
+        // A pair's CTAs each load half of the unit's columns (64-column chunks).
+        const bool one_head = un.half >= 0;
+        const int chunks = kPair ? (one_head ? 1 : 2) : R::B_CHUNKS;
+        const int col0 = un.n_blk * BN +
+                         (kPair ? (one_head ? un.half * 128 + sc.rank * 64 : sc.rank * 128) : 0);
+        const uint32_t stage_tx = kPair ? 2u * (A_STAGE_BYTES + chunks * B_CHUNK_BYTES)
+                                        : R::STAGE_TX;
         for (int kb = sc.kb0; kb < sc.kb1; ++kb) {
-            if (!fu_wait_parity(bar_empty + 8 * stage, phase ^ 1u, abort_flag, p.timeout_ns,
+            if (!fu_wait_parity(b.empty + 8 * stage, phase ^ 1u, abort_flag, p.timeout_ns,
                                 p.status, W_EMPTY)) {
                 ok = false;
                 break;
             }
-            const uint32_t full = bar_full + 8 * stage;
-            mbar_arrive_expect_tx(full, STAGE_TX);
-            tma_load_2d(a0 + stage * A_STAGE_BYTES, &p.tm_x, full, kb * BK, m_blk * BM);
-            const uint32_t bdst = b0 + stage * B_STAGE_BYTES;
+            const uint32_t adst = a0 + stage * A_STAGE_BYTES;
+            const uint32_t bdst = b0 + stage * R::B_STAGE_BYTES;
+            if (kPair) {
+                // Both CTAs' bytes are counted on the leader's barrier.
+                const uint32_t full = map_cluster_smem(b.full + 8 * stage, 0);
+                if (sc.rank == 0) mbar_arrive_expect_tx(b.full + 8 * stage, stage_tx);
+                tma_load_2d_pair(adst, &p.tm_x, full, kb * BK, row0);
+                for (int c = 0; c < chunks; ++c)
+                    tma_load_2d_pair(bdst + c * B_CHUNK_BYTES, &p.tm_w, full, col0 + c * 64,
+                                     kb * BK);
+            } else {
+                const uint32_t full = b.full + 8 * stage;
+                mbar_arrive_expect_tx(full, stage_tx);
+                tma_load_2d(adst, &p.tm_x, full, kb * BK, row0);
 #pragma unroll
-            for (int c = 0; c < BN / 64; ++c)
-                tma_load_2d(bdst + c * B_CHUNK_BYTES, &p.tm_w, full, n_blk * BN + c * 64, kb * BK);
+                for (int c = 0; c < R::B_CHUNKS; ++c)
+                    tma_load_2d(bdst + c * B_CHUNK_BYTES, &p.tm_w, full, col0 + c * 64, kb * BK);
+            }
             issued_mask |= 1u << stage;
             last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
-            if (++stage == STAGES) {
+            if (++stage == R::STAGES) {
                 stage = 0;
                 phase ^= 1u;
             }
         }
     }
     if (!ok) {
-        // Loads already issued must land before this CTA's shared memory is released.
-        for (int s = 0; s < STAGES; ++s)
-            if (issued_mask & (1u << s))
-                drain_wait(bar_full + 8 * s, (last_parity >> s) & 1u, p.timeout_ns, p.status);
+        if (kPair) {
+            // This CTA's loads are counted on the leader's barriers; give any
+            // still in flight time to land before shared memory is released.
+            const uint64_t t0 = globaltimer_ns();
+            while (globaltimer_ns() - t0 < 100000) {
+            }
+        } else {
+            // Loads already issued must land before this CTA's shared memory is released.
+            for (int s = 0; s < R::STAGES; ++s)
+                if (issued_mask & (1u << s))
+                    drain_wait(b.full + 8 * s, (last_parity >> s) & 1u, p.timeout_ns, p.status);
+        }
     }
 }
 
+template <bool kPair>
 __device__ void run_mma(const QkvParams& p, const Sched& sc, uint8_t* smem, uint32_t tmem_base,
-                        uint32_t bar_full, uint32_t bar_empty, uint32_t bar_tfull,
-                        uint32_t bar_tempty, uint32_t bar_mma_done, volatile int* abort_flag) {
-    constexpr uint32_t idesc = make_idesc_bf16_f32(BM, BN, /*a_mn_major=*/false,
-                                                   /*b_mn_major=*/true);
+                        const Bars& b, volatile int* abort_flag) {
+    using R = Ring<kPair>;
+    // kPair: M = 256 over the pair, each CTA's B holds N/2 = 128 columns.
+    constexpr uint32_t idesc_full = make_idesc_bf16_f32(kPair ? 2 * BM : BM, BN,
+                                                        /*a_mn_major=*/false,
+                                                        /*b_mn_major=*/true);
+    constexpr uint32_t idesc_head = make_idesc_bf16_f32(kPair ? 2 * BM : BM, BN / 2, false, true);
     const uint32_t a0 = smem_u32(smem + OFF_A);
-    const uint32_t b0 = smem_u32(smem + OFF_B);
+    const uint32_t b0 = smem_u32(smem + R::OFF_B);
     int stage = 0;
     uint32_t phase = 0;
     int local = 0;
@@ -210,22 +303,23 @@ __device__ void run_mma(const QkvParams& p, const Sched& sc, uint8_t* smem, uint
     for (int tile = sc.first; ok && tile < sc.end; tile += sc.stride, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!fu_wait_parity(bar_tempty + 8 * acc, acc_phase ^ 1u, abort_flag, p.timeout_ns,
+        if (!fu_wait_parity(b.tempty + 8 * acc, acc_phase ^ 1u, abort_flag, p.timeout_ns,
                             p.status, W_TEMPTY)) {
             ok = false;
             break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t idesc = decode_unit(p, tile).half >= 0 ? idesc_head : idesc_full;
         for (int kb = sc.kb0; kb < sc.kb1; ++kb) {
-            if (!fu_wait_parity(bar_full + 8 * stage, phase, abort_flag, p.timeout_ns, p.status,
+            if (!fu_wait_parity(b.full + 8 * stage, phase, abort_flag, p.timeout_ns, p.status,
                                 W_FULL)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             const uint32_t a_base = a0 + stage * A_STAGE_BYTES;
-            const uint32_t b_base = b0 + stage * B_STAGE_BYTES;
+            const uint32_t b_base = b0 + stage * R::B_STAGE_BYTES;
 #pragma unroll
             for (int k = 0; k < BK / UMMA_K; ++k) {
                 // A: K-major, 128B swizzle; K advances 32 bytes inside the swizzle row.
@@ -234,19 +328,35 @@ __device__ void run_mma(const QkvParams& p, const Sched& sc, uint8_t* smem, uint
                 // (leading offset), 8-row groups 1024 bytes apart (stride offset).
                 const uint64_t bdesc =
                     make_smem_desc_sw128(b_base + k * UMMA_K * 128, B_CHUNK_BYTES, 1024);
-                tc_mma_bf16(d_tmem, adesc, bdesc, idesc, (kb != sc.kb0 || k != 0) ? 1u : 0u);
+                const uint32_t accum = (kb != sc.kb0 || k != 0) ? 1u : 0u;
+                if (kPair)
+                    tc_mma_bf16_pair(d_tmem, adesc, bdesc, idesc, accum);
+                else
+                    tc_mma_bf16(d_tmem, adesc, bdesc, idesc, accum);
             }
-            tc_commit(bar_empty + 8 * stage);      // frees the stage when these MMAs finish
-            if (++stage == STAGES) {
+            // Frees the stage (in both CTAs of a pair) when these MMAs finish.
+            if (kPair)
+                tc_commit_pair_mc(b.empty + 8 * stage, 0x3);
+            else
+                tc_commit(b.empty + 8 * stage);
+            if (++stage == R::STAGES) {
                 stage = 0;
                 phase ^= 1u;
             }
         }
-        if (ok) tc_commit(bar_tfull + 8 * acc);    // accumulator ready for the epilogue
+        if (ok) {                                   // accumulator ready for the epilogue
+            if (kPair)
+                tc_commit_pair_mc(b.tfull + 8 * acc, 0x3);
+            else
+                tc_commit(b.tfull + 8 * acc);
+        }
     }
     // Every MMA this thread issued must finish before TMEM is released.
-    tc_commit(bar_mma_done);
-    drain_wait(bar_mma_done, 0, p.timeout_ns, p.status);
+    if (kPair)
+        tc_commit_pair_mc(b.mma_done, 0x1);
+    else
+        tc_commit(b.mma_done);
+    drain_wait(b.mma_done, 0, p.timeout_ns, p.status);
 }
 
 // Position of token row m, clamped (and reported) when outside the cache.
@@ -389,9 +499,10 @@ __device__ __forceinline__ void emit_head(const QkvParams& p, uint32_t taddr, in
     }
 }
 
+template <bool kPair>
 __device__ void run_epilogue(const QkvParams& p, const Sched& sc, uint8_t* smem,
-                             uint32_t tmem_base, uint32_t bar_tfull, uint32_t bar_tempty,
-                             const float* gam, volatile int* abort_flag) {
+                             uint32_t tmem_base, const Bars& b, const float* gam,
+                             volatile int* abort_flag) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int quarter = warp & 3;           // TMEM lanes this warp may access
@@ -404,9 +515,11 @@ __device__ void run_epilogue(const QkvParams& p, const Sched& sc, uint8_t* smem,
     for (int tile = sc.first; tile < sc.end; tile += sc.stride, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        const int m_blk = tile / p.num_n_blocks;
-        const int n_blk = tile % p.num_n_blocks;
-        const int m = m_blk * BM + row_in_tile;
+        const Unit un = decode_unit(p, tile);
+        const int m_blk = un.m_blk;
+        const int n_blk = un.n_blk;
+        const int row_base = m_blk * sc.rows_per_tile + sc.rank * BM;
+        const int m = row_base + row_in_tile;
         const bool row_valid = m < p.L;
         // This row's cos|sin, fetched while the tensor cores still work on the
         // tile (shared by both heads).
@@ -420,19 +533,25 @@ __device__ void run_epilogue(const QkvParams& p, const Sched& sc, uint8_t* smem,
                 sinv[i] = __ldg(rope_row + 16 + i);
             }
         }
-        if (!fu_wait_parity(bar_tfull + 8 * acc, acc_phase, abort_flag, p.timeout_ns, p.status,
+        if (!fu_wait_parity(b.tfull + 8 * acc, acc_phase, abort_flag, p.timeout_ns, p.status,
                             W_TFULL))
             break;
         tc_fence_after();
-        const int heads_here = min(2, p.heads - n_blk * 2);   // odd head count: last tile has one
+        // Heads of this unit: both of the tile (odd head count: the last tile
+        // has one), or the single head of a one-head unit (accumulator column 0).
+        const int h0 = n_blk * 2 + (un.half >= 0 ? un.half : 0);
+        const int heads_here = un.half >= 0 ? (h0 < p.heads ? 1 : 0) : min(2, p.heads - h0);
 #pragma unroll 1
         for (int hs = 0; hs < heads_here; ++hs)
-            emit_head(p, tmem_base + lane_addr + acc * BN + hs * 128, n_blk * 2 + hs, m,
-                      row_valid, m_blk * BM + quarter * 32, cosv, sinv, gam, box_lo, box_hi,
-                      lane);
-        // Both heads of this accumulator have been read: hand TMEM back.
+            emit_head(p, tmem_base + lane_addr + acc * BN + hs * 128, h0 + hs, m, row_valid,
+                      row_base + quarter * 32, cosv, sinv, gam, box_lo, box_hi, lane);
+        // Both heads of this accumulator have been read: hand TMEM back (to
+        // the pair leader's MMA issuer, which counts both CTAs' threads).
         tc_fence_before();
-        mbar_arrive(bar_tempty + 8 * acc);
+        if (kPair && sc.rank != 0)
+            mbar_arrive_remote(map_cluster_smem(b.tempty + 8 * acc, 0));
+        else
+            mbar_arrive(b.tempty + 8 * acc);
     }
     if (lane == 0) {
         bulk_wait_all();                    // peer writes performed
@@ -445,13 +564,12 @@ __device__ void run_epilogue(const QkvParams& p, const Sched& sc, uint8_t* smem,
 // accumulator of the tile in its own shared memory (the operand ring, idle by
 // now), rows of PART_STRIDE bytes.  Only warps holding valid rows copy.
 __device__ void run_split_partial(const QkvParams& p, const Sched& sc, uint8_t* smem,
-                                  uint32_t tmem_base, uint32_t bar_tfull,
-                                  volatile int* abort_flag) {
+                                  uint32_t tmem_base, const Bars& b, volatile int* abort_flag) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int quarter = warp & 3;
     const int m_blk = sc.first / p.num_n_blocks;
-    if (!fu_wait_parity(bar_tfull, 0, abort_flag, p.timeout_ns, p.status, W_TFULL)) return;
+    if (!fu_wait_parity(b.tfull, 0, abort_flag, p.timeout_ns, p.status, W_TFULL)) return;
     tc_fence_after();
     if (m_blk * BM + quarter * 32 >= p.L) return;          // no valid row in this warp
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
@@ -582,36 +700,33 @@ __device__ void run_split_reduce(const QkvParams& p, const Sched& sc, uint8_t* s
 }
 
 // ------------------------------------------------------------ kernel
+template <bool kPair>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
+    using R = Ring<kPair>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const Sched sc = make_sched(p);
-    const bool split_mode = p.splits > 1;
-
-    const uint32_t bar_base = smem_u32(smem + OFF_BAR);
-    const uint32_t bar_full = bar_base;
-    const uint32_t bar_empty = bar_base + 8 * STAGES;
-    const uint32_t bar_tfull = bar_base + 16 * STAGES;
-    const uint32_t bar_tempty = bar_tfull + 16;
-    const uint32_t bar_mma_done = bar_tempty + 16;
+    const Sched sc = make_sched<kPair>(p);
+    const bool split_mode = !kPair && p.splits > 1;
+    const Bars b(smem_u32(smem + OFF_BAR));
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
     float* gam = reinterpret_cast<float*>(smem + OFF_GAMMA);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(bar_full + 8 * s, 1);
-            mbar_init(bar_empty + 8 * s, 1);
+        for (int s = 0; s < R::STAGES; ++s) {
+            mbar_init(b.full + 8 * s, 1);
+            mbar_init(b.empty + 8 * s, 1);
         }
         for (int a = 0; a < 2; ++a) {
-            mbar_init(bar_tfull + 8 * a, 1);
-            mbar_init(bar_tempty + 8 * a, NUM_EPI_THREADS);
+            mbar_init(b.tfull + 8 * a, 1);
+            // A pair's leader counts the epilogue threads of both CTAs.
+            mbar_init(b.tempty + 8 * a, kPair ? 2 * NUM_EPI_THREADS : NUM_EPI_THREADS);
         }
-        mbar_init(bar_mma_done, 1);
+        mbar_init(b.mma_done, 1);
         *abort_flag = 0;
         fence_mbar_init();
         tma_prefetch_desc(&p.tm_x);
@@ -620,32 +735,45 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
     for (int i = threadIdx.x; i < 256; i += NUM_THREADS)
         gam[i] = i < 128 ? p.q_gamma[i] : p.k_gamma[i - 128];
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
-        tmem_relinquish();
+        if (kPair) {
+            tmem_alloc_pair(smem_u32(tmem_holder), TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    // A pair's barriers and TMEM must exist in both CTAs before either uses them.
+    if (kPair) cluster_sync_all();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
 
     if (warp == 0) {
-        if (lane == 0) run_producer(p, sc, smem, bar_full, bar_empty, abort_flag);
+        if (lane == 0) run_producer<kPair>(p, sc, smem, b, abort_flag);
         __syncwarp();
     } else if (warp == 1) {
-        if (lane == 0)
-            run_mma(p, sc, smem, tmem_base, bar_full, bar_empty, bar_tfull, bar_tempty,
-                    bar_mma_done, abort_flag);
+        if (lane == 0 && (!kPair || sc.rank == 0))
+            run_mma<kPair>(p, sc, smem, tmem_base, b, abort_flag);
         __syncwarp();
     } else if (split_mode) {
-        run_split_partial(p, sc, smem, tmem_base, bar_tfull, abort_flag);
+        run_split_partial(p, sc, smem, tmem_base, b, abort_flag);
     } else {
-        run_epilogue(p, sc, smem, tmem_base, bar_tfull, bar_tempty, gam, abort_flag);
+        run_epilogue<kPair>(p, sc, smem, tmem_base, b, gam, abort_flag);
     }
 
     tc_fence_before();
     __syncthreads();
+    // Both CTAs of a pair are done with TMEM (reads and the leader's MMAs).
+    if (kPair) cluster_sync_all();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+    if (warp == 1) {
+        if (kPair)
+            tmem_dealloc_pair(tmem_base, TMEM_COLS);
+        else
+            tmem_dealloc(tmem_base, TMEM_COLS);
+    }
 
     if (split_mode) {
         // Every CTA of the cluster reaches both barriers on every path, so a
@@ -655,7 +783,6 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
         cluster_sync_all();                 // peers are done reading this CTA's partial
     }
 
-    // ---- exit barrier: the last CTA of this rank joins the SP group.
     // Every CTA's output is complete (stores waited for, then the barriers
     // above).  A world of one needs only GPU scope; with peers, one
     // system-scope fence per CTA makes its remote stores visible beyond this
@@ -737,6 +864,7 @@ struct fu_qkv_ctx {
     fu_qkv_topology topo;
     int sm_count = 0;
     int max_clusters[9] = {0};    // co-resident clusters of each size (index = CTAs per cluster)
+    int max_pairs = 0;            // co-resident CTA pairs of the pair variant
     uint32_t epoch = 0;
     int last_grid = 0;
     // Tensor-map caches.
@@ -815,8 +943,11 @@ extern "C" int fu_qkv_create(const fu_qkv_topology* topo, fu_qkv_ctx** out) {
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(topo->device);
-    cudaError_t e = cudaFuncSetAttribute(fused_qkv_exchange_kernel,
+    cudaError_t e = cudaFuncSetAttribute(fused_qkv_exchange_kernel<false>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(fused_qkv_exchange_kernel<true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC);
     cudaSetDevice(prev);
     if (e != cudaSuccess)
         return set_error(FU_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
@@ -835,11 +966,21 @@ extern "C" int fu_qkv_create(const fu_qkv_topology* topo, fu_qkv_ctx** out) {
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, fused_qkv_exchange_kernel, &cfg) != cudaSuccess) {
+        if (cudaOccupancyMaxActiveClusters(&n, fused_qkv_exchange_kernel<false>, &cfg) !=
+            cudaSuccess) {
             cudaGetLastError();
             n = 0;
         }
         ctx->max_clusters[cs] = n;
+        if (cs == 2) {
+            n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, fused_qkv_exchange_kernel<true>, &cfg) !=
+                cudaSuccess) {
+                cudaGetLastError();
+                n = 0;
+            }
+            ctx->max_pairs = n;
+        }
     }
     cudaSetDevice(prev);
     ctx->topo = *topo;
@@ -961,14 +1102,40 @@ extern "C" int fu_qkv_forward(fu_qkv_ctx* ctx, const void* x, const void* w,
 
     p.splits = choose_splits(ctx, tiles, p.k_blocks, L < BM ? L : BM,
                              static_cast<int>((flags >> 8) & 0xFu));
-    const int grid = p.splits > 1 ? static_cast<int>(tiles) * p.splits
-                                  : static_cast<int>(tiles < ctx->sm_count ? tiles : ctx->sm_count);
+    // CTA pairs (256-row tiles) for the persistent grid once a call spans two
+    // row blocks, unless the flags pin the variant.
+    const uint32_t variant = (flags >> 12) & 0x3u;
+    const bool pair = p.splits == 1 && ctx->max_pairs > 0 &&
+                      (variant == 2u || (variant == 0u && m_blocks >= 2));
+    int grid;
+    p.num_units = p.num_tiles;
+    p.full_units = p.num_tiles;
+    if (pair) {
+        // Whole tiles fill full rounds of the co-resident pairs; a partial last
+        // round that at most half fills them is re-tiled into one-head units.
+        const int64_t T = (L + 2 * BM - 1) / (2 * BM) * p.num_n_blocks;
+        const int64_t P = ctx->max_pairs;
+        const int64_t rem = T % P;
+        int64_t units = T, full = T;
+        if (rem > 0 && 2 * rem <= P && (flags & FU_FWD_NO_RETILE) == 0) {
+            full = T - rem;
+            units = T + rem;
+        }
+        p.num_tiles = static_cast<int32_t>(T);
+        p.num_units = static_cast<int32_t>(units);
+        p.full_units = static_cast<int32_t>(full);
+        grid = 2 * static_cast<int>(units < P ? units : P);
+    } else if (p.splits > 1) {
+        grid = static_cast<int>(tiles) * p.splits;
+    } else {
+        grid = static_cast<int>(tiles < ctx->sm_count ? tiles : ctx->sm_count);
+    }
     ctx->last_grid = grid;
     int prev = 0;
     cudaGetDevice(&prev);
     if (prev != t.device) cudaSetDevice(t.device);
     cudaError_t e;
-    if (p.splits > 1) {
+    if (pair || p.splits > 1) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(grid, 1, 1);
         cfg.blockDim = dim3(NUM_THREADS, 1, 1);
@@ -976,15 +1143,16 @@ extern "C" int fu_qkv_forward(fu_qkv_ctx* ctx, const void* x, const void* w,
         cfg.stream = static_cast<cudaStream_t>(stream);
         cudaLaunchAttribute attr;
         attr.id = cudaLaunchAttributeClusterDimension;
-        attr.val.clusterDim.x = p.splits;
+        attr.val.clusterDim.x = pair ? 2 : p.splits;
         attr.val.clusterDim.y = 1;
         attr.val.clusterDim.z = 1;
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, fused_qkv_exchange_kernel, p);
+        e = pair ? cudaLaunchKernelEx(&cfg, fused_qkv_exchange_kernel<true>, p)
+                 : cudaLaunchKernelEx(&cfg, fused_qkv_exchange_kernel<false>, p);
     } else {
-        fused_qkv_exchange_kernel<<<grid, NUM_THREADS, SMEM_ALLOC,
-                                    static_cast<cudaStream_t>(stream)>>>(p);
+        fused_qkv_exchange_kernel<false><<<grid, NUM_THREADS, SMEM_ALLOC,
+                                           static_cast<cudaStream_t>(stream)>>>(p);
         e = cudaGetLastError();
     }
     if (prev != t.device) cudaSetDevice(prev);
@@ -1036,7 +1204,7 @@ static void noalloc_setup(int device, NoallocDevice& st) {
                  device, cudaGetErrorString(e));
         return;
     }
-    e = cudaFuncSetAttribute(fused_qkv_exchange_kernel,
+    e = cudaFuncSetAttribute(fused_qkv_exchange_kernel<false>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_ALLOC);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount,
                                                      device);
@@ -1153,6 +1321,8 @@ extern "C" int fu_qkv_forward_noalloc(int device, const void* x, const void* w,
     p.num_n_blocks = (heads + 1) / 2;
     const int64_t tiles = (L + BM - 1) / BM * p.num_n_blocks;
     p.num_tiles = static_cast<int32_t>(tiles);
+    p.num_units = p.num_tiles;
+    p.full_units = p.num_tiles;
     p.k_blocks = static_cast<int32_t>(hidden_size / BK);
     p.q_eps = static_cast<float>(q_epsilon);
     p.k_eps = static_cast<float>(k_epsilon);
@@ -1166,7 +1336,7 @@ extern "C" int fu_qkv_forward_noalloc(int device, const void* x, const void* w,
     cudaError_t e = cudaMemsetAsync(st.scratch + FU_SYNC_COUNTER, 0, sizeof(uint32_t), s);
     if (e != cudaSuccess) return set_error(FU_ERR_CUDA, "clearing scratch: %s", cudaGetErrorString(e));
     const int grid = static_cast<int>(tiles < st.sm_count ? tiles : st.sm_count);
-    fused_qkv_exchange_kernel<<<grid, NUM_THREADS, SMEM_ALLOC, s>>>(p);
+    fused_qkv_exchange_kernel<false><<<grid, NUM_THREADS, SMEM_ALLOC, s>>>(p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(FU_ERR_CUDA, "launch failed: %s", cudaGetErrorString(e));
     return FU_OK;

@@ -71,6 +71,15 @@ enum fu_device_status {
  * reduced by a cluster of n CTAs that sum their partials over distributed
  * shared memory; 1 forces the persistent one-CTA-per-tile grid. */
 #define FU_FWD_SPLITS(n) (((uint32_t)(n) & 0xFu) << 8)
+/* Persistent-grid variant: 0 = automatic (CTA pairs once a call spans two
+ * 128-row blocks), FU_FWD_SINGLE = one CTA per 128 x 256 tile, FU_FWD_PAIR =
+ * CTA pairs (tcgen05 cta_group::2) on 256 x 256 tiles. */
+#define FU_FWD_SINGLE (1u << 12)
+#define FU_FWD_PAIR (2u << 12)
+/* Keep whole 2-head tiles in the last round of the pair grid (by default a
+ * last round that at most half fills the pairs is re-tiled into one-head
+ * units). */
+#define FU_FWD_NO_RETILE (1u << 14)
 
 FU_API const char* fu_last_error(void);
 FU_API int fu_version(void);

@@ -38,9 +38,10 @@ def oracle_topology(cfg):
                            cfg.hidden_size)
 
 
-def run_group(cfg, tokens, tp_rank=0, seed=0, splits=0):
+def run_group(cfg, tokens, tp_rank=0, seed=0, splits=0, variant=0):
     """Emulate SP group ``tp_rank`` of ``cfg`` on one GPU; return everything the
-    checks need.  ``splits`` forces the split-K factor (0: automatic)."""
+    checks need.  ``splits`` forces the split-K factor (0: automatic),
+    ``variant`` the persistent-grid variant (FU_FWD_SINGLE / FU_FWD_PAIR)."""
     topo = oracle_topology(cfg)
     xs, pos, params = make_world(cfg, tokens, seed=seed)
     S = cfg.sp_size
@@ -55,7 +56,7 @@ def run_group(cfg, tokens, tp_rank=0, seed=0, splits=0):
         dumps = [torch.empty(tokens, topo.packed_width, dtype=torch.bfloat16, device=dev)
                  for _ in ranks]
         group.run(gx, gp, gparams, gemm_outs=dumps,
-                  flags=_C.FU_FWD_NO_PEER_WAIT | _C.FU_FWD_SPLITS(splits))
+                  flags=_C.FU_FWD_NO_PEER_WAIT | _C.FU_FWD_SPLITS(splits) | variant)
         torch.cuda.synchronize()
         assert group.status.value == 0, _C.decode_status(group.status.value)
         assert group.flags_ok()
@@ -159,6 +160,29 @@ def test_split_k_cluster_reduction(tokens, splits):
     check_group(run_group(cfg, tokens, splits=splits))
 
 
+@pytest.mark.parametrize("tokens,variant", [
+    (1, "pair"), (65, "pair"), (128, "pair"), (129, "pair"), (256, "pair"), (300, "pair"),
+    (1024, "pair"), (1024, "single"), (300, "single"), (1024, "pair_whole"), (4096, "pair"),
+])
+def test_persistent_variants(tokens, variant):
+    """Persistent grid with one CTA per 128x256 tile, and with CTA pairs
+    (tcgen05 cta_group::2, 256x256 tiles, each CTA holding half of W)."""
+    base = CONFIGS["c1"]
+    cfg = base.__class__("c1_p1", 1, 1, base.hidden_size, base.num_heads, base.num_kv_heads,
+                         base.tokens, base.max_position)
+    flag = {"pair": _C.FU_FWD_PAIR, "single": _C.FU_FWD_SINGLE,
+            "pair_whole": _C.FU_FWD_PAIR | _C.FU_FWD_NO_RETILE}[variant]
+    check_group(run_group(cfg, tokens, splits=1, variant=flag))
+
+
+@pytest.mark.parametrize("cfg_name,tokens,tp_rank,variant", [
+    ("c3", 300, 1, "pair"), ("c1", 257, 0, "pair"), ("c0", 130, 0, "pair"),
+])
+def test_persistent_variants_emulated_groups(cfg_name, tokens, tp_rank, variant):
+    flag = _C.FU_FWD_PAIR if variant == "pair" else _C.FU_FWD_SINGLE
+    check_group(run_group(CONFIGS[cfg_name], tokens, tp_rank=tp_rank, splits=1, variant=flag))
+
+
 @pytest.mark.parametrize("cfg_name,tokens,tp_rank,splits", [
     ("c3", 1, 1, 8), ("c3", 129, 0, 4), ("c1", 64, 0, 2), ("c0", 64, 0, 3),
 ])
@@ -195,11 +219,13 @@ def exact_world(S, H, q_heads, kv_heads, tokens, seed=0):
     return xs, pos, [params] * S
 
 
-@pytest.mark.parametrize("S,H,q,kv,tokens,splits", [
-    (1, 256, 4, 2, 65, 1), (2, 256, 4, 2, 65, 1), (4, 512, 8, 4, 130, 1), (2, 128, 2, 2, 1, 1),
-    (1, 64, 1, 1, 200, 1), (2, 256, 4, 2, 65, 4), (4, 512, 8, 4, 130, 3), (1, 512, 4, 2, 1, 8),
+@pytest.mark.parametrize("S,H,q,kv,tokens,splits,variant", [
+    (1, 256, 4, 2, 65, 1, 0), (2, 256, 4, 2, 65, 1, 0), (4, 512, 8, 4, 130, 1, 0),
+    (2, 128, 2, 2, 1, 1, 0), (1, 64, 1, 1, 200, 1, 0), (2, 256, 4, 2, 65, 4, 0),
+    (4, 512, 8, 4, 130, 3, 0), (1, 512, 4, 2, 1, 8, 0), (2, 256, 4, 2, 300, 1, 2 << 12),
+    (1, 64, 1, 1, 200, 1, 2 << 12), (4, 512, 8, 4, 130, 1, 1 << 12),
 ])
-def test_bit_exact_on_exact_inputs(S, H, q, kv, tokens, splits):
+def test_bit_exact_on_exact_inputs(S, H, q, kv, tokens, splits, variant):
     """Placement, padding, norm, RoPE and clipping, bit for bit."""
     xs, pos, params = exact_world(S, H, q, kv, tokens)
     topo = oracle.Topology(S, S, q, kv, H)
@@ -210,7 +236,7 @@ def test_bit_exact_on_exact_inputs(S, H, q, kv, tokens, splits):
     try:
         group.run([x.to(dev) for x in xs], [p.to(dev) for p in pos],
                   [to_device(p, dev) for p in params],
-                  flags=_C.FU_FWD_NO_PEER_WAIT | _C.FU_FWD_SPLITS(splits))
+                  flags=_C.FU_FWD_NO_PEER_WAIT | _C.FU_FWD_SPLITS(splits) | variant)
         torch.cuda.synchronize()
         assert group.status.value == 0
         assert group.flags_ok()
