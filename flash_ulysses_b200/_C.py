@@ -19,7 +19,9 @@ FU_MAX_SP = 8
 FU_HEAD_DIM = 128
 FU_IPC_HANDLE_BYTES = 64
 FU_SYNC_WORDS = 64
+FU_SYNC_ENTRY = 8
 FU_SYNC_COUNTER = 32
+FU_SYNC_EPOCH = 33
 FU_FWD_NO_PEER_WAIT = 1
 
 

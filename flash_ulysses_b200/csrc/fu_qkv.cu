@@ -19,10 +19,14 @@
 //               staged in swizzled shared memory and written by TMA bulk
 //               tensor stores directly into the destination rank's receive
 //               buffer (a peer GPU's memory mapped into this process).
-// A tile is 128 token rows x 2 heads (256 packed columns).  After its last
-// tile every CTA waits for its stores to complete and bumps a per-rank
-// counter; the last CTA of the rank publishes the call's epoch into every SP
-// member's flag word and waits (bounded) for theirs.
+// A tile is 128 token rows x 2 heads (256 packed columns).  Each call's epoch
+// lives in the rank's sync block and is advanced by the kernel itself.  At
+// start the call announces the epoch to its SP peers (entry flags); before a
+// CTA's first store into a peer's buffer it waits until every peer has
+// started the same call (so the peer's stream has finished with the previous
+// outputs).  After its last tile every CTA waits for its stores to complete
+// and bumps a per-rank counter; the last CTA of the rank publishes the epoch
+// into every SP member's exit flag and waits (bounded) for theirs.
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -102,7 +106,6 @@ struct __align__(64) QkvParams {
     int32_t sp_size, sp_rank, q_per_gpu, kv_per_gpu;
     int32_t num_n_blocks, num_tiles, k_blocks;
     float q_eps, k_eps;
-    uint32_t epoch;
     uint32_t wait_peers;
     int32_t splits;                         // >1: split-K over a cluster of this many CTAs
     void* out_base[3 * FU_MAX_SP];          // receive buffers (split mode stores rows directly)
@@ -214,6 +217,25 @@ struct Bars {
         : full(base), empty(base + 8 * MAX_STAGES), tfull(base + 16 * MAX_STAGES),
           tempty(base + 16 * MAX_STAGES + 16), mma_done(base + 16 * MAX_STAGES + 32) {}
 };
+
+// Entry barrier, run by the 4 epilogue warps before their CTA's first store
+// into a peer's buffer: one thread waits (bounded) until every SP member has
+// started this call's epoch, then the warps meet on named barrier 1.
+__device__ __forceinline__ void wait_peers_entered(const QkvParams& p, uint32_t epoch) {
+    if (p.sp_size > 1 && p.wait_peers && threadIdx.x == 64) {
+        const uint32_t* entry = p.sync[p.sp_rank] + FU_SYNC_ENTRY;
+        const uint64_t t0 = globaltimer_ns();
+        for (int s = 0; s < p.sp_size; ++s) {
+            while (static_cast<int32_t>(ld_acquire_sys_u32(entry + s) - epoch) < 0) {
+                if (globaltimer_ns() - t0 > p.timeout_ns) {
+                    report_status(p.status, FU_DEV_PEER_TIMEOUT, 16 + s);
+                    break;
+                }
+            }
+        }
+    }
+    named_bar_sync(1, NUM_EPI_THREADS);
+}
 
 // ------------------------------------------------------------ roles
 template <bool kPair>
@@ -502,7 +524,7 @@ __device__ __forceinline__ void emit_head(const QkvParams& p, uint32_t taddr, in
 template <bool kPair>
 __device__ void run_epilogue(const QkvParams& p, const Sched& sc, uint8_t* smem,
                              uint32_t tmem_base, const Bars& b, const float* gam,
-                             volatile int* abort_flag) {
+                             volatile int* abort_flag, uint32_t epoch) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int quarter = warp & 3;           // TMEM lanes this warp may access
@@ -510,6 +532,7 @@ __device__ void run_epilogue(const QkvParams& p, const Sched& sc, uint8_t* smem,
     uint8_t* box_lo = smem + OFF_STG + (warp - 2) * STAGING_PER_WARP;
     uint8_t* box_hi = box_lo + BOX_BYTES;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    wait_peers_entered(p, epoch);
 
     int local = 0;
     for (int tile = sc.first; tile < sc.end; tile += sc.stride, ++local) {
@@ -675,7 +698,8 @@ __device__ __forceinline__ void split_item_emit(const QkvParams& p, const float4
 }
 
 __device__ void run_split_reduce(const QkvParams& p, const Sched& sc, uint8_t* smem,
-                                 const float* gam) {
+                                 const float* gam, uint32_t epoch) {
+    wait_peers_entered(p, epoch);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int m_blk = sc.first / p.num_n_blocks;
@@ -716,7 +740,15 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
     float* gam = reinterpret_cast<float*>(smem + OFF_GAMMA);
 
+    uint32_t* my_sync = p.sync[p.sp_rank];
+    uint32_t* epoch_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC + 8);
     if (threadIdx.x == 0) {
+        // This call's epoch: one past the last call's (the kernel advances it).
+        const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my_sync + FU_SYNC_EPOCH) + 1;
+        *epoch_slot = epoch;
+        if (blockIdx.x == 0 && p.sp_size > 1)
+            for (int d = 0; d < p.sp_size; ++d)
+                st_release_sys_u32(p.sync[d] + FU_SYNC_ENTRY + p.sp_rank, epoch);
         for (int s = 0; s < R::STAGES; ++s) {
             mbar_init(b.full + 8 * s, 1);
             mbar_init(b.empty + 8 * s, 1);
@@ -749,6 +781,7 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
     if (kPair) cluster_sync_all();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
+    const uint32_t epoch = *epoch_slot;
 
     if (warp == 0) {
         if (lane == 0) run_producer<kPair>(p, sc, smem, b, abort_flag);
@@ -760,7 +793,7 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
     } else if (split_mode) {
         run_split_partial(p, sc, smem, tmem_base, b, abort_flag);
     } else {
-        run_epilogue<kPair>(p, sc, smem, tmem_base, b, gam, abort_flag);
+        run_epilogue<kPair>(p, sc, smem, tmem_base, b, gam, abort_flag, epoch);
     }
 
     tc_fence_before();
@@ -779,7 +812,7 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
         // Every CTA of the cluster reaches both barriers on every path, so a
         // CTA that gave up on a wait cannot strand its peers here.
         cluster_sync_all();                 // partials visible cluster-wide
-        if (warp >= 2) run_split_reduce(p, sc, smem, gam);
+        if (warp >= 2) run_split_reduce(p, sc, smem, gam, epoch);
         cluster_sync_all();                 // peers are done reading this CTA's partial
     }
 
@@ -790,23 +823,25 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
     // epoch (cumulative over every counted CTA).
     if (threadIdx.x == 64) {
         const bool aborted = *abort_flag != 0;
-        uint32_t* my_sync = p.sync[p.sp_rank];
         if (p.sp_size > 1) fence_acq_rel_sys(); else fence_acq_rel_gpu();
         const uint32_t old =
             atom_add_acq_rel_gpu_u32(my_sync + FU_SYNC_COUNTER, aborted ? 0x10001u : 1u);
         if ((old & 0xFFFFu) == gridDim.x - 1) {
+            // Last CTA: every CTA has read the epoch, so it can advance, and
+            // the counter is ready for the next call.
             const bool any_abort = aborted || (old >> 16) != 0;
             *reinterpret_cast<volatile uint32_t*>(my_sync + FU_SYNC_COUNTER) = 0u;
+            *reinterpret_cast<volatile uint32_t*>(my_sync + FU_SYNC_EPOCH) = epoch;
             if (!any_abort) {
                 if (p.sp_size == 1) {
-                    st_release_gpu_u32(my_sync, p.epoch);
+                    st_release_gpu_u32(my_sync, epoch);
                 } else {
                     for (int d = 0; d < p.sp_size; ++d)
-                        st_release_sys_u32(p.sync[d] + p.sp_rank, p.epoch);
+                        st_release_sys_u32(p.sync[d] + p.sp_rank, epoch);
                     if (p.wait_peers) {
                         const uint64_t t0 = globaltimer_ns();
                         for (int s = 0; s < p.sp_size; ++s) {
-                            while (static_cast<int32_t>(ld_acquire_sys_u32(my_sync + s) - p.epoch) <
+                            while (static_cast<int32_t>(ld_acquire_sys_u32(my_sync + s) - epoch) <
                                    0) {
                                 if (globaltimer_ns() - t0 > p.timeout_ns) {
                                     report_status(p.status, FU_DEV_PEER_TIMEOUT, s);
@@ -1096,8 +1131,7 @@ extern "C" int fu_qkv_forward(fu_qkv_ctx* ctx, const void* x, const void* w,
     p.k_blocks = static_cast<int32_t>(H / BK);
     p.q_eps = static_cast<float>(q_epsilon);
     p.k_eps = static_cast<float>(k_epsilon);
-    p.epoch = ++ctx->epoch;
-    if (p.epoch == 0) p.epoch = ++ctx->epoch;   // 0 is the flags' initial value
+    ++ctx->epoch;                                // calls launched (the device keeps the epoch)
     p.wait_peers = (flags & FU_FWD_NO_PEER_WAIT) ? 0u : 1u;
 
     p.splits = choose_splits(ctx, tiles, p.k_blocks, L < BM ? L : BM,
@@ -1326,10 +1360,9 @@ extern "C" int fu_qkv_forward_noalloc(int device, const void* x, const void* w,
     p.k_blocks = static_cast<int32_t>(hidden_size / BK);
     p.q_eps = static_cast<float>(q_epsilon);
     p.k_eps = static_cast<float>(k_epsilon);
-    // Any epoch works for a world of one: the kernel publishes its own flag
-    // before it reads it.  Only the completion counter must start at zero.
-    p.epoch = ++st.epoch;
-    if (p.epoch == 0) p.epoch = ++st.epoch;
+    // The kernel advances the epoch word of the scratch itself; only the
+    // completion counter must start at zero.
+    ++st.epoch;
     p.wait_peers = 1u;
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -43,10 +43,18 @@ extern "C" {
 /* Per-rank synchronisation block (uint32 words), shared with the SP group:
  *   [0, FU_MAX_SP)            exit flags: word p holds the last epoch SP member
  *                             p finished writing into this rank
+ *   [FU_SYNC_ENTRY, +FU_MAX_SP) entry flags: word p holds the last epoch SP
+ *                             member p started (its stream reached the call)
  *   [FU_SYNC_COUNTER]         CTA completion counter (local use only)
+ *   [FU_SYNC_EPOCH]           this rank's epoch: the number of calls made,
+ *                             advanced by the kernel itself, so captured CUDA
+ *                             graphs replay with fresh epochs
+ * Calls of one SP group advance in lockstep: every rank makes the same calls.
  */
 #define FU_SYNC_WORDS 64
+#define FU_SYNC_ENTRY 8
 #define FU_SYNC_COUNTER 32
+#define FU_SYNC_EPOCH 33
 
 enum fu_error {
     FU_OK = 0,
@@ -66,7 +74,7 @@ enum fu_device_status {
 };
 
 /* Flags for fu_qkv_forward. */
-#define FU_FWD_NO_PEER_WAIT 1u  /* signal peers but do not wait for them */
+#define FU_FWD_NO_PEER_WAIT 1u  /* publish entry/exit flags but wait for no peer */
 /* Split-K factor 1..8 (0 = choose automatically): with n > 1 each tile is
  * reduced by a cluster of n CTAs that sum their partials over distributed
  * shared memory; 1 forces the persistent one-CTA-per-tile grid. */
@@ -162,7 +170,8 @@ FU_API int fu_qkv_forward(fu_qkv_ctx* ctx, const void* x, const void* w, const i
                    int64_t local_tokens, int64_t rope_rows, double q_epsilon,
                    double k_epsilon, uint32_t flags, void* stream, void* gemm_out);
 
-/* Epoch of the most recent call (the value written into peers' flags). */
+/* Number of calls launched through this context (the device-side epoch of
+ * the most recent call once it has run, for contexts used without graphs). */
 FU_API uint32_t fu_qkv_epoch(const fu_qkv_ctx* ctx);
 
 /* Number of CTAs the most recent call launched (persistent grid). */

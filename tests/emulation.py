@@ -75,13 +75,19 @@ class EmulatedGroup:
         return [tuple(b[:rows] for b in bufs) for bufs in self.recv]
 
     def flags_ok(self):
-        """Every member published this call's epoch to every member."""
+        """Every member advanced its epoch to this call's and published it to
+        every member (entry and exit flags); completion counters are reset."""
         epoch = self.ops[0].epoch
         for d in range(self.S):
-            words = self.sync[d][: self.S].cpu()
-            if not bool((words == epoch).all()):
+            block = self.sync[d].cpu()
+            if int(block[_C.FU_SYNC_EPOCH]) != epoch:
                 return False
-            if int(self.sync[d][_C.FU_SYNC_COUNTER].item()) != 0:
+            if not bool((block[: self.S] == epoch).all()):
+                return False
+            if self.S > 1 and not bool(
+                    (block[_C.FU_SYNC_ENTRY: _C.FU_SYNC_ENTRY + self.S] == epoch).all()):
+                return False
+            if int(block[_C.FU_SYNC_COUNTER]) != 0:
                 return False
         return True
 

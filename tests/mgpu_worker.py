@@ -135,6 +135,58 @@ def run_case(cfg, tokens_list, gloo, *, cpu_check_max=256):
     return failures
 
 
+def graph_replay_case(gloo):
+    """Each rank captures calls in a CUDA graph and replays them with no host
+    rendezvous in between: device-side epochs and the entry barrier keep the
+    ranks in step and keep a fast rank from overwriting data a slow rank's
+    stream has not reached."""
+    rank, world = dist.get_rank(), dist.get_world_size()
+    cfg = Config("graph", world, world, 4096, 32, 8, (257,), 32768)
+    topo = oracle.Topology(world, world, 32, 8, 4096)
+    nccl_sp = sp_groups(world, world, "nccl")
+    ctx = FlashUlyssesContext(rank=rank, world_size=world, max_local_tokens=257,
+                              hidden_size=4096, num_heads=32, num_kv_heads=8, sp_size=world,
+                              control_group=gloo, timeout_s=10.0)
+    failures = []
+    try:
+        xs, pos, params = make_world(cfg, 257, seed=11)
+        gp = {k: (v.cuda() if torch.is_tensor(v) else v) for k, v in params[rank].items()}
+        x, p = xs[rank].cuda(), pos[rank].cuda()
+        want = reference_gpu(topo, x, p, gp, nccl_sp)
+        torch.cuda.synchronize()
+        dist.barrier(group=gloo)
+        ctx.ulysses_qkv_forward(x, gp["qkv_weight"], p, gp["q_norm_weight"],
+                                gp["k_norm_weight"], gp["rope_cache"])
+        ctx.check()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s), torch.cuda.graph(graph, stream=s):
+            for _ in range(4):
+                got = ctx.ulysses_qkv_forward(x, gp["qkv_weight"], p, gp["q_norm_weight"],
+                                              gp["k_norm_weight"], gp["rope_cache"])
+        torch.cuda.current_stream().wait_stream(s)
+        dist.barrier(group=gloo)
+        for _ in range(6):
+            graph.replay()                     # no rendezvous between replays
+        ctx.check()
+        epoch = int(ctx.barrier.data_[33].item())
+        if epoch != 1 + 4 * 6:
+            failures.append(f"rank {rank}: device epoch {epoch}, expected 25")
+        for g, w, name in zip(got, want, "QKV"):
+            bad = int((~torch.isclose(g.float(), w.float(), atol=ATOL, rtol=RTOL)).sum())
+            if bad > max(1, 2e-6 * g.numel()):
+                failures.append(f"graph replay {name}: {bad} violations")
+        log(f"  CUDA graph replay x6 (4 calls each, no rendezvous): "
+            f"{'ok' if not failures else failures}")
+        del graph
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier(group=gloo)
+        ctx.close()
+    return failures
+
+
 def exact_placement_case(world, sp, gloo):
     """Bit-exact placement/padding/capacity on exact inputs over real peer memory."""
     from test_gpu_kernel import exact_world
@@ -224,6 +276,7 @@ def main():
     try:
         for cfg in cases:
             failures += run_case(cfg, list(cfg.tokens), gloo)
+        failures += graph_replay_case(gloo)
         failures += exact_placement_case(world, world, gloo)
         if world >= 4:
             failures += exact_placement_case(world, world // 2, gloo)

@@ -51,7 +51,7 @@ def test_error_channel_without_gpu():
 def test_constants_match_header():
     text = HEADER.read_text()
     for name in ("FU_MAX_SP", "FU_HEAD_DIM", "FU_IPC_HANDLE_BYTES", "FU_SYNC_WORDS",
-                 "FU_SYNC_COUNTER"):
+                 "FU_SYNC_ENTRY", "FU_SYNC_COUNTER", "FU_SYNC_EPOCH"):
         m = re.search(rf"#define {name} (\d+)", text)
         assert m and int(m.group(1)) == getattr(_C, name), name
 

@@ -315,3 +315,42 @@ def test_context_api_single_gpu():
         assert ctx.epoch == 3
     finally:
         ctx.close()
+
+
+def test_cuda_graph_replay_advances_device_epoch():
+    """Calls captured in a CUDA graph replay with fresh epochs: the kernel
+    advances the epoch in the sync block itself."""
+    from flash_ulysses_b200 import FlashUlyssesContext
+
+    base = CONFIGS["c1"]
+    cfg = base.__class__("c1_p1", 1, 1, 1024, 8, 2, (96,), 4096)
+    torch.cuda.set_device(0)
+    ctx = FlashUlyssesContext(rank=0, world_size=1, max_local_tokens=96, hidden_size=1024,
+                              num_heads=8, num_kv_heads=2, sp_size=1)
+    try:
+        xs, pos, params = make_world(cfg, 96, seed=3)
+        gp = to_device(params[0], "cuda")
+        x, p = xs[0].cuda(), pos[0].cuda()
+        ctx.ulysses_qkv_forward(x, positions=p, **gp)      # warm-up outside capture
+        ctx.check()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s), torch.cuda.graph(graph, stream=s):
+            for _ in range(3):
+                q, k, v = ctx.ulysses_qkv_forward(x, positions=p, **gp)
+        torch.cuda.current_stream().wait_stream(s)
+        for replay in range(4):
+            for t in (ctx.Q, ctx.K, ctx.V):
+                t.data_.fill_(float("nan"))
+            graph.replay()
+            ctx.check()
+            epoch = int(ctx.barrier.data_[_C.FU_SYNC_EPOCH].item())
+            assert epoch == 1 + 3 * (replay + 1), epoch     # warm-up + 3 per replay
+            want = oracle.simulate_world(oracle_topology(cfg), xs, pos, params)[0]
+            for got, exp in zip((q, k, v), want):
+                bad, err = isclose_stats(got, exp)
+                assert bad <= 1, (bad, err)
+        del graph
+    finally:
+        ctx.close()
