@@ -30,7 +30,11 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "fused QKV+exchange latency ms (max rank) vs L; GEMM TFLOP/s/GPU vs peak"
-HIDDEN, Q_HEADS, KV_HEADS, MAX_POS = 4096, 32, 8, 32768
+# Per-rank model shapes of the benchmark configurations: hidden size, query and
+# key/value heads of one base-TP group, RoPE table rows.  c1/c2 (Qwen3-8B-like),
+# c3 (the same model at base TP 2: half the heads per rank), c4 (Qwen3-32B-like).
+SHAPES = {"c1": (4096, 32, 8, 32768), "c3": (4096, 16, 4, 32768), "c4": (5120, 64, 8, 131072)}
+HIDDEN, Q_HEADS, KV_HEADS, MAX_POS = SHAPES["c1"]
 ROTATE = 4            # distinct input sets cycled per step: 4 x 82 MB > 126 MB L2
 SWEEP = (1, 128, 1024, 4096, 8192)
 
@@ -44,7 +48,12 @@ def parse():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    return ap.parse_args()
+    ap.add_argument("--shape", choices=sorted(SHAPES), default="c1",
+                    help="per-rank model shape (default c1: H=4096, 32/8 heads)")
+    args = ap.parse_args()
+    global HIDDEN, Q_HEADS, KV_HEADS, MAX_POS
+    HIDDEN, Q_HEADS, KV_HEADS, MAX_POS = SHAPES[args.shape]
+    return args
 
 
 def dist_env():
@@ -274,8 +283,8 @@ def reference_arm(args):
 
 def workload_config(n, tokens):
     return {
-        "workload": f"H={HIDDEN} Q/KV={Q_HEADS}/{KV_HEADS} head_dim=128, world=sp={n} "
-                    f"(c1 shape; N=4 is c1, N=8 is c2), L={tokens} tokens/GPU",
+        "workload": f"H={HIDDEN} Q/KV={Q_HEADS}/{KV_HEADS} (per base-TP group) head_dim=128, "
+                    f"world=sp={n} (default c1 shape; N=4 is c1, N=8 is c2), L={tokens} tokens/GPU",
         "hidden_size": HIDDEN, "num_heads": Q_HEADS, "num_kv_heads": KV_HEADS,
         "tokens_per_gpu": tokens, "world_size": n, "sp_size": n, "base_tp": 1,
         "global_tokens": tokens * n,
