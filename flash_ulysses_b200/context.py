@@ -161,6 +161,7 @@ class FlashUlyssesContext:
         *,
         q_epsilon=1e-6,
         k_epsilon=1e-6,
+        _projection_out=None,
     ):
         """Return BF16 (q, k, v), each with L * sp_size rows.
 
@@ -169,6 +170,9 @@ class FlashUlyssesContext:
         positions int64 [L], norm weights FP32 [128], and a NeoX RoPE cache
         FP32 [max_position, 128] containing [cos(64), sin(64)]. Positions must
         index the cache. Epsilons must be positive. The caller crops padding.
+
+        ``_projection_out`` is test instrumentation: a BF16 [L, packed_width]
+        tensor that also receives this rank's BF16 projection ``x @ W``.
         """
         local_tokens = hidden_states.size(0)
         if not 0 < local_tokens <= self.max_local_tokens:
@@ -177,7 +181,8 @@ class FlashUlyssesContext:
             raise RuntimeError("an earlier call failed on the device: "
                                + _C.decode_status(self._status.value))
         _C.launch(hidden_states, qkv_weight, positions, q_norm_weight, k_norm_weight,
-                  rope_cache, self._op, q_epsilon=q_epsilon, k_epsilon=k_epsilon)
+                  rope_cache, self._op, q_epsilon=q_epsilon, k_epsilon=k_epsilon,
+                  gemm_out=_projection_out)
         output_tokens = local_tokens * self.sp_size
         return tuple(t.data()[:output_tokens] for t in (self.Q, self.K, self.V))
 
