@@ -28,6 +28,7 @@ FU_FWD_NO_PEER_WAIT = 1
 FU_FWD_SINGLE = 1 << 12
 FU_FWD_PAIR = 2 << 12
 FU_FWD_NO_RETILE = 1 << 14
+FU_FWD_FP32_EPILOGUE = 1 << 15
 
 
 def FU_FWD_SPLITS(n):

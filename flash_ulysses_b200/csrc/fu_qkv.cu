@@ -107,6 +107,7 @@ struct __align__(64) QkvParams {
     int32_t num_n_blocks, num_tiles, k_blocks;
     float q_eps, k_eps;
     uint32_t wait_peers;
+    uint32_t fp32_epilogue;                 // 1: no BF16 rounding before the final store
     int32_t splits;                         // >1: split-K over a cluster of this many CTAs
     void* out_base[3 * FU_MAX_SP];          // receive buffers (split mode stores rows directly)
     int32_t num_units;                      // work units of the persistent grid
@@ -117,6 +118,10 @@ static_assert(sizeof(QkvParams) <= 4096, "kernel parameter block too large");
 
 __device__ __forceinline__ float bf16_round(float v) {
     return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+__device__ __forceinline__ float round_if(float v, bool to_bf16) {
+    return to_bf16 ? bf16_round(v) : v;
 }
 
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
@@ -429,8 +434,8 @@ __device__ __forceinline__ void emit_head(const QkvParams& p, uint32_t taddr, in
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-                const float2 f = unpack_bf16x2(pack_bf16x2(__uint_as_float(r[2 * i]),
-                                                           __uint_as_float(r[2 * i + 1])));
+                float2 f = make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+                if (!p.fp32_epilogue) f = unpack_bf16x2(pack_bf16x2(f.x, f.y));
                 ss = fmaf(f.x, f.x, ss);       // squares of BF16 values are exact in FP32
                 ss = fmaf(f.y, f.y, ss);
             }
@@ -444,26 +449,36 @@ __device__ __forceinline__ void emit_head(const QkvParams& p, uint32_t taddr, in
     __syncwarp();
 
     const float* g = gam + (comp < 2 ? comp : 0) * 128;
+    const bool r16 = !p.fp32_epilogue;          // the reference path's BF16 boundaries
 #pragma unroll
     for (int q = 0; q < 4; ++q) {               // columns 16q..16q+15 and 64+16q..
         uint32_t lo_raw[16], hi_raw[16];
         tmem_ld_16cols(taddr + 16 * q, lo_raw);
         tmem_ld_16cols(taddr + 64 + 16 * q, hi_raw);
         tmem_ld_wait();
-        uint32_t lo_p[8], hi_p[8];              // the BF16 projection (pairs of columns)
+        // The projection as the epilogue sees it: rounded to BF16 (reference
+        // PyTorch path) or the FP32 accumulator (FP32-intermediate mode).
+        float lo_v[16], hi_v[16];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            lo_p[i] = pack_bf16x2(__uint_as_float(lo_raw[2 * i]), __uint_as_float(lo_raw[2 * i + 1]));
-            hi_p[i] = pack_bf16x2(__uint_as_float(hi_raw[2 * i]), __uint_as_float(hi_raw[2 * i + 1]));
+        for (int i = 0; i < 16; ++i) {
+            lo_v[i] = round_if(__uint_as_float(lo_raw[i]), r16);
+            hi_v[i] = round_if(__uint_as_float(hi_raw[i]), r16);
         }
         if (p.gemm_out != nullptr && row_valid) {
             __nv_bfloat16* row = p.gemm_out + static_cast<int64_t>(m) * p.N + h * 128;
             uint4* dlo = reinterpret_cast<uint4*>(row + 16 * q);
             uint4* dhi = reinterpret_cast<uint4*>(row + 64 + 16 * q);
-            dlo[0] = make_uint4(lo_p[0], lo_p[1], lo_p[2], lo_p[3]);
-            dlo[1] = make_uint4(lo_p[4], lo_p[5], lo_p[6], lo_p[7]);
-            dhi[0] = make_uint4(hi_p[0], hi_p[1], hi_p[2], hi_p[3]);
-            dhi[1] = make_uint4(hi_p[4], hi_p[5], hi_p[6], hi_p[7]);
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                dlo[c] = make_uint4(pack_bf16x2(lo_v[8 * c], lo_v[8 * c + 1]),
+                                    pack_bf16x2(lo_v[8 * c + 2], lo_v[8 * c + 3]),
+                                    pack_bf16x2(lo_v[8 * c + 4], lo_v[8 * c + 5]),
+                                    pack_bf16x2(lo_v[8 * c + 6], lo_v[8 * c + 7]));
+                dhi[c] = make_uint4(pack_bf16x2(hi_v[8 * c], hi_v[8 * c + 1]),
+                                    pack_bf16x2(hi_v[8 * c + 2], hi_v[8 * c + 3]),
+                                    pack_bf16x2(hi_v[8 * c + 4], hi_v[8 * c + 5]),
+                                    pack_bf16x2(hi_v[8 * c + 6], hi_v[8 * c + 7]));
+            }
         }
         uint32_t olo[8], ohi[8];
         if (comp < 2) {
@@ -480,13 +495,14 @@ __device__ __forceinline__ void emit_head(const QkvParams& p, uint32_t taddr, in
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 const int j = 16 * q + 2 * i;
-                const float2 lo = unpack_bf16x2(lo_p[i]);
-                const float2 hi = unpack_bf16x2(hi_p[i]);
                 // RMSNorm, * gamma, BF16 boundary (torch_base.py:56-61).
-                const float nl0 = bf16_round(__fmul_rn(__fmul_rn(lo.x, scale), g[j]));
-                const float nl1 = bf16_round(__fmul_rn(__fmul_rn(lo.y, scale), g[j + 1]));
-                const float nh0 = bf16_round(__fmul_rn(__fmul_rn(hi.x, scale), g[j + 64]));
-                const float nh1 = bf16_round(__fmul_rn(__fmul_rn(hi.y, scale), g[j + 65]));
+                const float nl0 = round_if(__fmul_rn(__fmul_rn(lo_v[2 * i], scale), g[j]), r16);
+                const float nl1 =
+                    round_if(__fmul_rn(__fmul_rn(lo_v[2 * i + 1], scale), g[j + 1]), r16);
+                const float nh0 =
+                    round_if(__fmul_rn(__fmul_rn(hi_v[2 * i], scale), g[j + 64]), r16);
+                const float nh1 =
+                    round_if(__fmul_rn(__fmul_rn(hi_v[2 * i + 1], scale), g[j + 65]), r16);
                 // NeoX rotation, separately rounded products (torch_base.py:62-63).
                 const float c0 = cs[2 * i], c1 = cs[2 * i + 1];
                 const float s0 = sn[2 * i], s1 = sn[2 * i + 1];
@@ -498,8 +514,8 @@ __device__ __forceinline__ void emit_head(const QkvParams& p, uint32_t taddr, in
         } else {
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                olo[i] = lo_p[i];
-                ohi[i] = hi_p[i];
+                olo[i] = pack_bf16x2(lo_v[2 * i], lo_v[2 * i + 1]);
+                ohi[i] = pack_bf16x2(hi_v[2 * i], hi_v[2 * i + 1]);
             }
         }
         // 16-byte chunks 2q and 2q+1 of the row in each box (128-byte swizzle).
@@ -636,10 +652,13 @@ __device__ __forceinline__ void split_item_emit(const QkvParams& p, const float4
     // BF16 projection of columns 4l..4l+3 of head h, token row m.
     const uint32_t u0 = pack_bf16x2(acc.x, acc.y);
     const uint32_t u1 = pack_bf16x2(acc.z, acc.w);
+    const bool r16 = !p.fp32_epilogue;
     float v[4];
-    {
+    if (r16) {
         const float2 a = unpack_bf16x2(u0), b = unpack_bf16x2(u1);
         v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    } else {
+        v[0] = acc.x; v[1] = acc.y; v[2] = acc.z; v[3] = acc.w;
     }
     if (p.gemm_out != nullptr)
         *reinterpret_cast<uint2*>(p.gemm_out + static_cast<int64_t>(m) * p.N + h * 128 + 4 * lane) =
@@ -666,7 +685,7 @@ __device__ __forceinline__ void split_item_emit(const QkvParams& p, const float4
         const float* g = gam + comp * 128 + 4 * lane;
         float n[4], partner[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) n[i] = bf16_round(__fmul_rn(__fmul_rn(v[i], scale), g[i]));
+        for (int i = 0; i < 4; ++i) n[i] = round_if(__fmul_rn(__fmul_rn(v[i], scale), g[i]), r16);
 #pragma unroll
         for (int i = 0; i < 4; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, n[i], 16);
         int64_t pos = __ldg(p.positions + m);
@@ -1133,6 +1152,7 @@ extern "C" int fu_qkv_forward(fu_qkv_ctx* ctx, const void* x, const void* w,
     p.k_eps = static_cast<float>(k_epsilon);
     ++ctx->epoch;                                // calls launched (the device keeps the epoch)
     p.wait_peers = (flags & FU_FWD_NO_PEER_WAIT) ? 0u : 1u;
+    p.fp32_epilogue = (flags & FU_FWD_FP32_EPILOGUE) ? 1u : 0u;
 
     p.splits = choose_splits(ctx, tiles, p.k_blocks, L < BM ? L : BM,
                              static_cast<int>((flags >> 8) & 0xFu));

@@ -88,6 +88,11 @@ enum fu_device_status {
  * last round that at most half fills the pairs is re-tiled into one-head
  * units). */
 #define FU_FWD_NO_RETILE (1u << 14)
+/* Keep Q/K in FP32 from the accumulator through RMSNorm and RoPE and round to
+ * BF16 once at the end -- the numerics of the reference's Hopper kernel
+ * (flash_ulysses_kernel_hopper.cu:129-152).  Default: the reference PyTorch
+ * path's rounding points (BF16 projection, BF16 after the norm). */
+#define FU_FWD_FP32_EPILOGUE (1u << 15)
 
 FU_API const char* fu_last_error(void);
 FU_API int fu_version(void);

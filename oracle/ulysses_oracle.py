@@ -109,16 +109,41 @@ def norm_rope(y, gamma, epsilon, cos, sin):
     return rotated.bfloat16().flatten(1)
 
 
-def rank_send(topo: Topology, x, positions, params, projection=None):
+def norm_rope_fp32(y32, gamma, epsilon, cos, sin):
+    """Headwise RMSNorm then NeoX RoPE kept in FP32 from the accumulator, one
+    BF16 rounding at the end: the numerics of the reference's Hopper kernel
+    (flash_ulysses_kernel_hopper.cu:129-152: ``rsqrtf(sum/128 + eps)``,
+    ``mul_row``, ``mul_col``, rotation ``lo*c - hi*s`` / ``hi*c + lo*s`` built
+    with --fmad=false).  ``y32`` is the FP32 projection ``[L, heads*128]``."""
+    tokens = y32.size(0)
+    value = y32.reshape(tokens, -1, HEAD_DIM).float()
+    value = value * torch.rsqrt(value.square().mean(dim=-1, keepdim=True) + epsilon)
+    value = value * gamma
+    lo, hi = value.chunk(2, dim=-1)
+    rotated = torch.cat((lo * cos - hi * sin, hi * cos + lo * sin), dim=-1)
+    return rotated.bfloat16().flatten(1)
+
+
+def rank_send(topo: Topology, x, positions, params, projection=None, fp32_epilogue=False):
     """Per-rank compute before the exchange: returns the packed ``[S, L, N/S]``
     send buffer (torch_base.py:50-69).
 
     ``projection`` optionally replaces ``x @ W`` with a given BF16 ``[L, N]``
     tensor, so the epilogue can be checked on exactly the projection another
-    implementation produced."""
+    implementation produced.  ``fp32_epilogue`` selects the reference Hopper
+    kernel's numerics instead of its PyTorch path's (see ``norm_rope_fp32``);
+    the FP32 projection is then the exact sum rounded once to FP32."""
+    cos, sin = params["rope_cache"][positions].unsqueeze(1).chunk(2, dim=-1)
+    if fp32_epilogue:
+        y32 = (x.double() @ params["qkv_weight"].double()).float()
+        q, k, v = y32.split(topo.widths(), dim=-1)
+        q = norm_rope_fp32(q, params["q_norm_weight"], params["q_epsilon"], cos, sin)
+        k = norm_rope_fp32(k, params["k_norm_weight"], params["k_epsilon"], cos, sin)
+        v = v.bfloat16()
+        parts = [t.reshape(x.size(0), topo.sp_size, -1) for t in (q, k, v)]
+        return torch.cat(parts, dim=-1).transpose(0, 1).contiguous()
     y = project(x, params["qkv_weight"]) if projection is None else projection
     q, k, v = y.split(topo.widths(), dim=-1)
-    cos, sin = params["rope_cache"][positions].unsqueeze(1).chunk(2, dim=-1)
     q = norm_rope(q, params["q_norm_weight"], params["q_epsilon"], cos, sin)
     k = norm_rope(k, params["k_norm_weight"], params["k_epsilon"], cos, sin)
     parts = [t.reshape(x.size(0), topo.sp_size, -1) for t in (q, k, v)]
@@ -135,7 +160,8 @@ def unpack(topo: Topology, received, tokens):
     )
 
 
-def simulate_world(topo: Topology, xs, positions, params_by_rank, projections=None):
+def simulate_world(topo: Topology, xs, positions, params_by_rank, projections=None,
+                   fp32_epilogue=False):
     """Run every rank in one process.
 
     ``xs[r]``/``positions[r]`` are rank r's inputs; ``params_by_rank[r]`` its
@@ -149,7 +175,7 @@ def simulate_world(topo: Topology, xs, positions, params_by_rank, projections=No
     tokens = xs[0].size(0)
     sends = [
         rank_send(topo, xs[r], positions[r], params_by_rank[r],
-                  None if projections is None else projections[r])
+                  None if projections is None else projections[r], fp32_epilogue)
         for r in range(topo.world_size)
     ]
     outputs = []
