@@ -115,6 +115,24 @@ def _load():
 
 lib = _load()
 
+# The CPython fast-call binding of fu_qkv_forward, when it was built against
+# the library in use (it links the in-tree build).
+try:
+    if "FLASH_ULYSSES_B200_LIB" in os.environ:
+        raise ImportError("library path overridden")
+    from . import _fu_fast as _fast
+except ImportError:
+    _fast = None
+
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def current_stream_handle(device_index):
+    """The cudaStream_t of the current torch stream on `device_index`."""
+    if _raw_stream is not None:
+        return _raw_stream(device_index)
+    return torch.cuda.current_stream(device_index).cuda_stream
+
 
 def last_error():
     return lib.fu_last_error().decode(errors="replace")
@@ -260,6 +278,10 @@ class QkvOp:
     def forward(self, x, w, positions, q_gamma, k_gamma, rope, local_tokens, rope_rows,
                 q_eps, k_eps, flags=0, stream=None, gemm_out=None):
         """Launch one fused call; all tensor arguments are raw device pointers."""
+        if _fast is not None:
+            _fast.forward(self.handle, x, w, positions, q_gamma, k_gamma, rope, local_tokens,
+                          rope_rows, q_eps, k_eps, flags, stream, gemm_out)
+            return
         rc = lib.fu_qkv_forward(self.handle, x, w, positions, q_gamma, k_gamma, rope,
                                 local_tokens, rope_rows, q_eps, k_eps, flags, stream, gemm_out)
         if rc != FU_OK:
@@ -284,9 +306,9 @@ def launch(x, qkv_weight, positions, q_gamma, k_gamma, rope, op: QkvOp, *, q_eps
     """Tensor-level launch on the current stream (the role of the reference's
     ``_C.launch``, kernel_hopper.cu:305-353).  Inputs are trusted to be
     contiguous device tensors of the documented dtypes, as in the reference."""
-    stream = torch.cuda.current_stream(x.device).cuda_stream
+    stream = current_stream_handle(x.get_device())
     op.forward(x.data_ptr(), qkv_weight.data_ptr(), positions.data_ptr(), q_gamma.data_ptr(),
-               k_gamma.data_ptr(), rope.data_ptr(), x.size(0), rope.size(0), float(q_epsilon),
+               k_gamma.data_ptr(), rope.data_ptr(), x.shape[0], rope.shape[0], float(q_epsilon),
                float(k_epsilon), flags, stream,
                None if gemm_out is None else gemm_out.data_ptr())
 

@@ -58,6 +58,7 @@ class FlashUlyssesContext:
         self.max_local_tokens = max_local_tokens
         self._op = None
         self._status = None
+        self._views = {}
         self.Q = self.K = self.V = self.barrier = None
 
         if not 1 <= sp_size <= self.world_size <= 8 or self.world_size % sp_size:
@@ -174,7 +175,7 @@ class FlashUlyssesContext:
         ``_projection_out`` is test instrumentation: a BF16 [L, packed_width]
         tensor that also receives this rank's BF16 projection ``x @ W``.
         """
-        local_tokens = hidden_states.size(0)
+        local_tokens = hidden_states.shape[0]
         if not 0 < local_tokens <= self.max_local_tokens:
             raise ValueError("Input length must be within [1, max_local_tokens]")
         if self._status.value:
@@ -183,8 +184,12 @@ class FlashUlyssesContext:
         _C.launch(hidden_states, qkv_weight, positions, q_norm_weight, k_norm_weight,
                   rope_cache, self._op, q_epsilon=q_epsilon, k_epsilon=k_epsilon,
                   gemm_out=_projection_out)
-        output_tokens = local_tokens * self.sp_size
-        return tuple(t.data()[:output_tokens] for t in (self.Q, self.K, self.V))
+        views = self._views.get(local_tokens)
+        if views is None:
+            output_tokens = local_tokens * self.sp_size
+            views = tuple(t.data()[:output_tokens] for t in (self.Q, self.K, self.V))
+            self._views = {local_tokens: views}      # row views of the receive buffers
+        return views
 
     def check(self):
         """Synchronise the device and raise if any call reported a device-side error."""
@@ -205,6 +210,7 @@ class FlashUlyssesContext:
         torch.cuda.synchronize(self.device)
         if self.world_size > 1 or dist.is_initialized():
             dist.barrier(group=self.control_group)
+        self._views = {}
         with torch.cuda.device(self.device):
             if self._op is not None:
                 self._op.destroy()

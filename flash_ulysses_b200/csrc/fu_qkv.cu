@@ -921,10 +921,18 @@ struct fu_qkv_ctx {
     int max_pairs = 0;            // co-resident CTA pairs of the pair variant
     uint32_t epoch = 0;
     int last_grid = 0;
-    // Tensor-map caches.
-    const void* x_ptr = nullptr;
-    int64_t x_rows = -1;
-    const void* w_ptr = nullptr;
+    // Tensor-map caches: encoded maps of recently seen inputs (weights are
+    // typically one per layer, activations come from a few recycled buffers),
+    // replaced round-robin, and the receive-buffer maps of the last length.
+    struct MapEntry {
+        const void* ptr = nullptr;
+        int64_t rows = -1;
+        CUtensorMap map;
+    };
+    static constexpr int kXMaps = 8, kWMaps = 16;
+    MapEntry x_maps[kXMaps];
+    MapEntry w_maps[kWMaps];
+    int x_next = 0, w_next = 0;
     int64_t out_rows = -1;
     fu::QkvParams params;
 };
@@ -1081,20 +1089,40 @@ extern "C" int fu_qkv_forward(fu_qkv_ctx* ctx, const void* x, const void* w,
     const int heads = t.q_heads + 2 * t.kv_heads;
     const int64_t N = static_cast<int64_t>(heads) * FU_HEAD_DIM;
     int rc;
-    if (x != ctx->x_ptr || L != ctx->x_rows) {
-        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(L)};
-        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(H * 2)};
-        const cuuint32_t box[2] = {BK, BM};
-        if ((rc = encode(&p.tm_x, x, 2, dims, strides, box, "hidden_states")) != FU_OK) return rc;
-        ctx->x_ptr = x;
-        ctx->x_rows = L;
+    {
+        fu_qkv_ctx::MapEntry* hit = nullptr;
+        for (auto& e : ctx->x_maps)
+            if (e.ptr == x && e.rows == L) hit = &e;
+        if (hit == nullptr) {
+            hit = &ctx->x_maps[ctx->x_next];
+            ctx->x_next = (ctx->x_next + 1) % fu_qkv_ctx::kXMaps;
+            const cuuint64_t dims[2] = {static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(L)};
+            const cuuint64_t strides[1] = {static_cast<cuuint64_t>(H * 2)};
+            const cuuint32_t box[2] = {BK, BM};
+            hit->ptr = nullptr;
+            if ((rc = encode(&hit->map, x, 2, dims, strides, box, "hidden_states")) != FU_OK)
+                return rc;
+            hit->ptr = x;
+            hit->rows = L;
+        }
+        p.tm_x = hit->map;
     }
-    if (w != ctx->w_ptr) {
-        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(H)};
-        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(N * 2)};
-        const cuuint32_t box[2] = {64, BK};
-        if ((rc = encode(&p.tm_w, w, 2, dims, strides, box, "qkv_weight")) != FU_OK) return rc;
-        ctx->w_ptr = w;
+    {
+        fu_qkv_ctx::MapEntry* hit = nullptr;
+        for (auto& e : ctx->w_maps)
+            if (e.ptr == w) hit = &e;
+        if (hit == nullptr) {
+            hit = &ctx->w_maps[ctx->w_next];
+            ctx->w_next = (ctx->w_next + 1) % fu_qkv_ctx::kWMaps;
+            const cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(H)};
+            const cuuint64_t strides[1] = {static_cast<cuuint64_t>(N * 2)};
+            const cuuint32_t box[2] = {64, BK};
+            hit->ptr = nullptr;
+            if ((rc = encode(&hit->map, w, 2, dims, strides, box, "qkv_weight")) != FU_OK)
+                return rc;
+            hit->ptr = w;
+        }
+        p.tm_w = hit->map;
     }
     if (L != ctx->out_rows) {
         for (int comp = 0; comp < 3; ++comp) {
