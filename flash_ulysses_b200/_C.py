@@ -29,6 +29,7 @@ FU_FWD_SINGLE = 1 << 12
 FU_FWD_PAIR = 2 << 12
 FU_FWD_NO_RETILE = 1 << 14
 FU_FWD_FP32_EPILOGUE = 1 << 15
+FU_FWD_STREAMK = 1 << 16
 
 
 def FU_FWD_SPLITS(n):
