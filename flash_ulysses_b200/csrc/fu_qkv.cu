@@ -490,6 +490,30 @@ __device__ __forceinline__ const float* rope_row_for(const QkvParams& p, int m, 
     return p.rope + pos * 128;
 }
 
+// One half (cos or sin: 64 floats) of the rope rows of a warp's 32 token
+// rows, into registers of the lane that owns each row.  A row-per-lane load
+// would touch 32 cache lines per instruction; instead two rows per
+// instruction are copied with coalesced 16-byte cp.async into the warp's
+// staging boxes (8 KiB, 16-byte chunks XOR-swizzled by row so that the
+// row-per-lane reads hit distinct banks), then each lane reads its own row.
+// The staging boxes must be free (no bulk store still reading them).
+__device__ __forceinline__ void load_rope_half(const float* my_row, int off, uint32_t buf,
+                                               int lane, float4 (&out)[16]) {
+    const int c = lane & 15;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        const int r = 2 * k + (lane >> 4);
+        const float* src = reinterpret_cast<const float*>(
+            __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(my_row), r));
+        cp_async_16(buf + r * 256 + ((c ^ (r & 7)) << 4), src + off + 4 * c);
+    }
+    cp_async_wait_all();
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) out[i] = ld_shared_f4(buf + lane * 256 + ((i ^ (lane & 7)) << 4));
+    __syncwarp();
+}
+
 // Everything after the projection for one head row, read from TMEM lane
 // `taddr` (this thread's token row, the head's first column): optional
 // projection dump, RMSNorm + RoPE for Q/K (V as is), swizzled staging, and
@@ -657,13 +681,11 @@ __device__ void run_epilogue(const QkvParams& p, const Sched& sc, uint8_t* smem,
         // tile (shared by both heads).
         float4 cosv[16], sinv[16];
         {
-            const float4* rope_row =
-                reinterpret_cast<const float4*>(rope_row_for(p, m, row_valid));
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                cosv[i] = __ldg(rope_row + i);
-                sinv[i] = __ldg(rope_row + 16 + i);
-            }
+            const float* rope_row = rope_row_for(p, m, row_valid);
+            if (lane == 0) bulk_wait_read_all();       // staging boxes free
+            __syncwarp();
+            load_rope_half(rope_row, 0, smem_u32(box_lo), lane, cosv);
+            load_rope_half(rope_row, 64, smem_u32(box_lo), lane, sinv);
         }
         if (!fu_wait_parity(b.tfull + 8 * acc, acc_phase, abort_flag, p.timeout_ns, p.status,
                             W_TFULL))
