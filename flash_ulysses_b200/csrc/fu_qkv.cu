@@ -607,17 +607,27 @@ __device__ __forceinline__ void emit_head(const QkvParams& p, uint32_t taddr, in
                                   sinv[4 * q + 1].w, sinv[4 * q + 2].x, sinv[4 * q + 2].y,
                                   sinv[4 * q + 2].z, sinv[4 * q + 2].w, sinv[4 * q + 3].x,
                                   sinv[4 * q + 3].y, sinv[4 * q + 3].z, sinv[4 * q + 3].w};
+            // Gamma for columns 16q.. and 64+16q.. (same address in every lane: a
+            // broadcast, read as 16-byte vectors).
+            float gl[16], gh[16];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float4 a = reinterpret_cast<const float4*>(g + 16 * q)[i];
+                const float4 b4 = reinterpret_cast<const float4*>(g + 64 + 16 * q)[i];
+                gl[4 * i] = a.x; gl[4 * i + 1] = a.y; gl[4 * i + 2] = a.z; gl[4 * i + 3] = a.w;
+                gh[4 * i] = b4.x; gh[4 * i + 1] = b4.y; gh[4 * i + 2] = b4.z; gh[4 * i + 3] = b4.w;
+            }
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                const int j = 16 * q + 2 * i;
                 // RMSNorm, * gamma, BF16 boundary (torch_base.py:56-61).
-                const float nl0 = round_if(__fmul_rn(__fmul_rn(lo_v[2 * i], scale), g[j]), r16);
+                const float nl0 =
+                    round_if(__fmul_rn(__fmul_rn(lo_v[2 * i], scale), gl[2 * i]), r16);
                 const float nl1 =
-                    round_if(__fmul_rn(__fmul_rn(lo_v[2 * i + 1], scale), g[j + 1]), r16);
+                    round_if(__fmul_rn(__fmul_rn(lo_v[2 * i + 1], scale), gl[2 * i + 1]), r16);
                 const float nh0 =
-                    round_if(__fmul_rn(__fmul_rn(hi_v[2 * i], scale), g[j + 64]), r16);
+                    round_if(__fmul_rn(__fmul_rn(hi_v[2 * i], scale), gh[2 * i]), r16);
                 const float nh1 =
-                    round_if(__fmul_rn(__fmul_rn(hi_v[2 * i + 1], scale), g[j + 65]), r16);
+                    round_if(__fmul_rn(__fmul_rn(hi_v[2 * i + 1], scale), gh[2 * i + 1]), r16);
                 // NeoX rotation, separately rounded products (torch_base.py:62-63).
                 const float c0 = cs[2 * i], c1 = cs[2 * i + 1];
                 const float s0 = sn[2 * i], s1 = sn[2 * i + 1];
