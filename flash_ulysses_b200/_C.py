@@ -30,6 +30,9 @@ FU_FWD_PAIR = 2 << 12
 FU_FWD_NO_RETILE = 1 << 14
 FU_FWD_FP32_EPILOGUE = 1 << 15
 FU_FWD_STREAMK = 1 << 16
+FU_OPROJ_READY = FU_SYNC_WORDS
+FU_OPROJ_GATHER_ONLY = 1 << 20
+FU_OPROJ_GEMM_ONLY = 1 << 21
 
 
 def FU_FWD_SPLITS(n):
@@ -55,6 +58,8 @@ EXPORTED = (
     "fu_buffer_close", "fu_status_alloc", "fu_status_free",
     "fu_qkv_create", "fu_qkv_destroy", "fu_qkv_forward", "fu_qkv_epoch",
     "fu_qkv_last_grid", "fu_qkv_forward_noalloc",
+    "fu_oproj_sync_words", "fu_oproj_create", "fu_oproj_destroy", "fu_oproj_forward",
+    "fu_oproj_calls", "fu_oproj_last_grid",
 )
 
 
@@ -73,6 +78,26 @@ class Topology(ctypes.Structure):
         ("q_recv", ctypes.c_void_p * FU_MAX_SP),
         ("k_recv", ctypes.c_void_p * FU_MAX_SP),
         ("v_recv", ctypes.c_void_p * FU_MAX_SP),
+        ("sync", ctypes.c_void_p * FU_MAX_SP),
+        ("status", ctypes.c_void_p),
+        ("status_host", ctypes.c_void_p),
+        ("timeout_ns", ctypes.c_uint64),
+    ]
+
+
+class OprojTopology(ctypes.Structure):
+    """``fu_oproj_topology``."""
+
+    _fields_ = [
+        ("device", ctypes.c_int32),
+        ("sp_size", ctypes.c_int32),
+        ("sp_rank", ctypes.c_int32),
+        ("q_heads", ctypes.c_int32),
+        ("reserved0", ctypes.c_int32),
+        ("reserved1", ctypes.c_int32),
+        ("hidden_size", ctypes.c_int64),
+        ("max_local_tokens", ctypes.c_int64),
+        ("gather", ctypes.c_void_p * FU_MAX_SP),
         ("sync", ctypes.c_void_p * FU_MAX_SP),
         ("status", ctypes.c_void_p),
         ("status_host", ctypes.c_void_p),
@@ -106,6 +131,12 @@ def _load():
         "fu_qkv_forward_noalloc": (ctypes.c_int, [ctypes.c_int, vp, vp, vp, vp, vp, vp, i64, i64,
                                                   i32, i32, i64, ctypes.c_double,
                                                   ctypes.c_double, vp, vp, vp, vp, vp]),
+        "fu_oproj_sync_words": (i64, [i64]),
+        "fu_oproj_create": (ctypes.c_int, [ctypes.POINTER(OprojTopology), ctypes.POINTER(vp)]),
+        "fu_oproj_destroy": (ctypes.c_int, [vp]),
+        "fu_oproj_forward": (ctypes.c_int, [vp, vp, vp, i64, vp, u32, vp]),
+        "fu_oproj_calls": (u32, [vp]),
+        "fu_oproj_last_grid": (ctypes.c_int, [vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -302,6 +333,40 @@ class QkvOp:
             self.handle = None
 
 
+class OprojOp:
+    """Owner of one ``fu_oproj_ctx`` (inverse exchange + output projection)."""
+
+    def __init__(self, topology: OprojTopology):
+        handle = ctypes.c_void_p()
+        check(lib.fu_oproj_create(ctypes.byref(topology), ctypes.byref(handle)),
+              "fu_oproj_create")
+        self.handle = handle.value
+        self.topology = topology
+
+    def forward(self, attn, w_o, local_tokens, out, flags=0, stream=None):
+        """Launch one call; tensor arguments are raw device pointers."""
+        rc = lib.fu_oproj_forward(self.handle, attn, w_o, local_tokens, out, flags, stream)
+        if rc != FU_OK:
+            raise RuntimeError(f"fu_oproj_forward failed (code {rc}): {last_error()}")
+
+    @property
+    def calls(self):
+        return lib.fu_oproj_calls(self.handle)
+
+    @property
+    def last_grid(self):
+        return lib.fu_oproj_last_grid(self.handle)
+
+    def destroy(self):
+        if self.handle:
+            lib.fu_oproj_destroy(self.handle)
+            self.handle = None
+
+
+def oproj_sync_words(max_local_tokens):
+    return int(lib.fu_oproj_sync_words(max_local_tokens))
+
+
 def launch(x, qkv_weight, positions, q_gamma, k_gamma, rope, op: QkvOp, *, q_epsilon,
            k_epsilon, flags=0, gemm_out=None):
     """Tensor-level launch on the current stream (the role of the reference's
@@ -315,7 +380,8 @@ def launch(x, qkv_weight, positions, q_gamma, k_gamma, rope, op: QkvOp, *, q_eps
 
 
 __all__ = [
-    "lib", "Topology", "ParallelTensor", "StatusWord", "QkvOp", "launch", "check",
+    "lib", "Topology", "OprojTopology", "ParallelTensor", "StatusWord", "QkvOp", "OprojOp",
+    "oproj_sync_words", "launch", "check",
     "decode_status", "tensor_from_device_ptr", "EXPORTED", "LIB_PATH",
 ]
 

@@ -22,7 +22,7 @@ CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 LIB_NAME = "libflash_ulysses_b200.so"
 LIB_PATH = PKG / LIB_NAME
-SOURCES = ["fu_capi.cu", "fu_qkv.cu"]
+SOURCES = ["fu_capi.cu", "fu_qkv.cu", "fu_oproj.cu"]
 FAST_SOURCE = "fu_pyfast.cpp"
 FAST_PATH = PKG / ("_fu_fast" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

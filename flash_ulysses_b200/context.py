@@ -49,6 +49,7 @@ class FlashUlyssesContext:
         sp_size=2,
         control_group=None,
         timeout_s=5.0,
+        output_projection=False,
     ):
         self.rank, self.world_size = rank, world_size
         self.control_group = control_group
@@ -57,9 +58,11 @@ class FlashUlyssesContext:
         self.head_dim, self.sp_size = head_dim, sp_size
         self.max_local_tokens = max_local_tokens
         self._op = None
+        self._oproj = None
         self._status = None
         self._views = {}
         self.Q = self.K = self.V = self.barrier = None
+        self.G = self.o_barrier = None
 
         if not 1 <= sp_size <= self.world_size <= 8 or self.world_size % sp_size:
             raise ValueError("SP must divide a single-node world of 1 to 8 GPUs")
@@ -116,6 +119,29 @@ class FlashUlyssesContext:
         topo.status_host = self._status.host_ptr
         topo.timeout_ns = int(timeout_s * 1e9)
         self._op = _C.QkvOp(topo)
+
+        if output_projection:
+            if hidden_size % 256:
+                raise ValueError("output_projection requires hidden_size divisible by 256")
+            # Gather buffer (peers push this rank's rows of their heads into it)
+            # and a separate synchronisation block with per-m-block ready counters.
+            self.G = parallel((max_local_tokens, self.local_q_heads * head_dim), torch.bfloat16)
+            self.o_barrier = parallel((_C.oproj_sync_words(max_local_tokens),), torch.int32)
+            self.o_barrier.data_.zero_()
+            otopo = _C.OprojTopology()
+            otopo.device = self.device.index
+            otopo.sp_size = sp_size
+            otopo.sp_rank = self.sp_rank
+            otopo.q_heads = self.local_q_heads
+            otopo.hidden_size = hidden_size
+            otopo.max_local_tokens = max_local_tokens
+            for i, r in enumerate(peers):
+                otopo.gather[i] = self.G.peer_ptr(r)
+                otopo.sync[i] = self.o_barrier.peer_ptr(r)
+            otopo.status = self._status.device_ptr
+            otopo.status_host = self._status.host_ptr
+            otopo.timeout_ns = int(timeout_s * 1e9)
+            self._oproj = _C.OprojOp(otopo)
 
         torch.cuda.current_stream(self.device).synchronize()
         if world_size > 1 or dist.is_initialized():
@@ -191,6 +217,40 @@ class FlashUlyssesContext:
             self._views = {local_tokens: views}      # row views of the receive buffers
         return views
 
+    @torch.no_grad()
+    def ulysses_o_proj_forward(self, attn_output, o_proj_weight, *, out=None):
+        """Inverse Ulysses exchange fused with the attention output projection
+        (no counterpart in the reference, which stops at the forward exchange).
+
+        ``attn_output`` is this rank's attention output, BF16
+        ``[L * sp_size, output_q_heads * 128]`` in the layout of the ``q``
+        returned by ``ulysses_qkv_forward`` (rows ``s*L..`` belong to SP member
+        ``s``); ``o_proj_weight`` is BF16 ``[hidden_size, local_q_heads * 128]``
+        (nn.Linear layout).  Returns BF16 ``[L, hidden_size]`` =
+        ``gathered @ o_proj_weight.T`` for this rank's L tokens, written into
+        ``out`` when given.  Requires ``output_projection=True`` at
+        construction; every rank of the SP group makes the same calls.
+        ``attn_output`` is only read during this rank's call.
+        """
+        if self._oproj is None:
+            raise RuntimeError("construct the context with output_projection=True")
+        rows = attn_output.shape[0]
+        if rows % self.sp_size:
+            raise ValueError("attn_output rows must be a multiple of sp_size")
+        local_tokens = rows // self.sp_size
+        if not 0 < local_tokens <= self.max_local_tokens:
+            raise ValueError("Input length must be within [1, max_local_tokens]")
+        if self._status.value:
+            raise RuntimeError("an earlier call failed on the device: "
+                               + _C.decode_status(self._status.value))
+        if out is None:
+            out = torch.empty(local_tokens, self.hidden_size, dtype=torch.bfloat16,
+                              device=self.device)
+        stream = _C.current_stream_handle(self.device.index)
+        self._oproj.forward(attn_output.data_ptr(), o_proj_weight.data_ptr(), local_tokens,
+                            out.data_ptr(), 0, stream)
+        return out
+
     def check(self):
         """Synchronise the device and raise if any call reported a device-side error."""
         torch.cuda.synchronize(self.device)
@@ -202,6 +262,8 @@ class FlashUlyssesContext:
         (call only when no launch of this context is in flight)."""
         torch.cuda.synchronize(self.device)
         self.barrier.data_[_C.FU_SYNC_COUNTER].zero_()
+        if self.o_barrier is not None:
+            self.o_barrier.data_[_C.FU_SYNC_COUNTER].zero_()
         torch.cuda.synchronize(self.device)
         self._status.clear()
 
@@ -215,7 +277,10 @@ class FlashUlyssesContext:
             if self._op is not None:
                 self._op.destroy()
                 self._op = None
-            for name in ("Q", "K", "V", "barrier"):
+            if self._oproj is not None:
+                self._oproj.destroy()
+                self._oproj = None
+            for name in ("Q", "K", "V", "barrier", "G", "o_barrier"):
                 t = getattr(self, name)
                 if t is not None:
                     t.close()

@@ -217,6 +217,74 @@ FU_API int fu_qkv_forward_noalloc(int device, const void* x, const void* w,
                                   double k_epsilon, void* q_out, void* k_out, void* v_out,
                                   int32_t* status, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Inverse exchange fused with the attention output projection.  No
+ * counterpart in the reference, which stops at the forward exchange; this is
+ * the step its outputs feed once attention has run (reference README.md:44-46
+ * describes the head <-> sequence exchange this inverts).
+ *
+ * SP member d holds attention output for its q_heads/S heads over the whole
+ * group's sequence, attn_d BF16 [S * L, q_heads/S * 128] (rows s*L.. belong to
+ * source s: the layout in which fu_qkv_forward delivers Q).  Each call returns
+ * to every source s its L rows for all q_heads local heads and multiplies them
+ * by the output projection:
+ *     out_s = G_s . W_o^T,   G_s [L, q_heads * 128],   W_o BF16 [H, q_heads * 128]
+ * (torch.nn.Linear's weight layout), FP32 accumulation, BF16 out [L, H].
+ * Each rank pushes its own attention output into the owners' gather buffers
+ * over NVLink while the owners' tensor cores start on the m-blocks already
+ * complete.
+ * ------------------------------------------------------------------------ */
+typedef struct fu_oproj_ctx fu_oproj_ctx;
+
+/* First word of the per-m-block ready counters in an o-projection sync block. */
+#define FU_OPROJ_READY FU_SYNC_WORDS
+/* Two-phase mode for SP ranks emulated on one GPU (whose kernels must not
+ * wait for one another): one call per rank with FU_OPROJ_GATHER_ONLY, then
+ * one per rank with FU_OPROJ_GEMM_ONLY.  Use with FU_FWD_NO_PEER_WAIT. */
+#define FU_OPROJ_GATHER_ONLY (1u << 20)
+#define FU_OPROJ_GEMM_ONLY (1u << 21)
+
+typedef struct fu_oproj_topology {
+    int32_t device;           /* CUDA device ordinal of this rank */
+    int32_t sp_size;          /* S: 1..FU_MAX_SP */
+    int32_t sp_rank;          /* this rank's index in its SP group */
+    int32_t q_heads;          /* local (post base-TP) query heads, divisible by S */
+    int32_t reserved0;
+    int32_t reserved1;
+    int64_t hidden_size;      /* H, a positive multiple of 256 */
+    int64_t max_local_tokens; /* largest L of any call */
+    /* Gather buffer of SP member p as mapped in this process: BF16
+     * [max_local_tokens, q_heads * 128], 16-byte aligned; peers write their
+     * columns into it (a member's own columns are read from its attn). */
+    void* gather[FU_MAX_SP];
+    /* O-projection sync block of SP member p (fu_oproj_sync_words words,
+     * zero-initialised), separate from the forward operator's. */
+    uint32_t* sync[FU_MAX_SP];
+    int32_t* status;          /* device pointer of a status word, may be NULL */
+    int32_t* status_host;     /* host view of the same word, may be NULL */
+    uint64_t timeout_ns;      /* bound on every device-side wait; 0 = 5 s */
+} fu_oproj_topology;
+
+/* Words of an o-projection sync block for calls of up to max_local_tokens. */
+FU_API int64_t fu_oproj_sync_words(int64_t max_local_tokens);
+FU_API int fu_oproj_create(const fu_oproj_topology* topo, fu_oproj_ctx** out);
+FU_API int fu_oproj_destroy(fu_oproj_ctx* ctx);
+
+/* One call, one launch on `stream`:
+ *   attn   BF16 [S * local_tokens, q_heads/S * 128], this rank's attention output
+ *   w_o    BF16 [H, q_heads * 128]
+ *   out    BF16 [local_tokens, H]
+ * Every rank of the SP group makes the same sequence of calls.  attn is read
+ * during this rank's call only, so it may be overwritten once the call has
+ * completed on this rank's stream. */
+FU_API int fu_oproj_forward(fu_oproj_ctx* ctx, const void* attn, const void* w_o,
+                            int64_t local_tokens, void* out, uint32_t flags, void* stream);
+
+/* Number of calls launched through this context. */
+FU_API uint32_t fu_oproj_calls(const fu_oproj_ctx* ctx);
+/* Number of CTAs the most recent call launched. */
+FU_API int fu_oproj_last_grid(const fu_oproj_ctx* ctx);
+
 #ifdef __cplusplus
 }
 #endif

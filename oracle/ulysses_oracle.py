@@ -33,6 +33,11 @@ Two entry points:
 * ``rank_forward_gloo`` is the per-rank form that calls
   ``torch.distributed.all_to_all_single`` on a (gloo) SP group, as the
   reference does with NCCL.
+
+For the output side (no counterpart in the reference, which stops at the
+forward exchange): ``inverse_exchange_world`` / ``o_proj_world`` and the
+per-rank ``rank_o_proj_gloo`` return each source's rows for all of its local
+heads and apply the output projection with FP32 accumulation.
 """
 
 from __future__ import annotations
@@ -195,6 +200,45 @@ def rank_forward_gloo(topo: Topology, x, positions, params, group):
     received = torch.empty_like(send)
     torch.distributed.all_to_all_single(received, send, group=group)
     return unpack(topo, received, x.size(0))
+
+
+def inverse_exchange_world(topo: Topology, attn_outs, tokens):
+    """Inverse of the forward exchange for Q-shaped tensors: every rank's
+    ``[S*L, output_q_heads*128]`` attention output (rows ``s*L..`` belong to
+    source ``s``, the layout ``unpack`` returns for Q) goes back to its
+    sources.  Returns, per rank, ``[L, local_q_heads*128]`` with member ``d``'s
+    heads in columns ``d*cols..`` -- the local head order of the forward's
+    projection (reference torch_base.py:68-76 run backwards; the reference
+    itself has no inverse step)."""
+    S = topo.sp_size
+    out = []
+    for r in range(topo.world_size):
+        start = r // S * S
+        src = r - start
+        out.append(torch.cat([attn_outs[start + d][src * tokens:(src + 1) * tokens]
+                              for d in range(S)], dim=-1))
+    return out
+
+
+def o_proj(gathered, o_weight):
+    """``F.linear(gathered, o_weight)`` with FP32 accumulation and one BF16
+    rounding (``o_weight`` is ``[H, local_q_heads*128]``, nn.Linear layout)."""
+    return (gathered.float() @ o_weight.float().t()).bfloat16()
+
+
+def o_proj_world(topo: Topology, attn_outs, o_weights, tokens):
+    """Inverse exchange then output projection for every rank of a world."""
+    gathered = inverse_exchange_world(topo, attn_outs, tokens)
+    return [o_proj(g, o_weights[r]) for r, g in enumerate(gathered)]
+
+
+def rank_o_proj_gloo(topo: Topology, attn_out, o_weight, tokens, group):
+    """Per-rank form over a process group: ``all_to_all_single`` sends block
+    ``s`` of the attention output (source ``s``'s rows) to member ``s``."""
+    send = attn_out.reshape(topo.sp_size, tokens, -1).contiguous()
+    received = torch.empty_like(send)
+    torch.distributed.all_to_all_single(received, send, group=group)
+    return o_proj(torch.cat(list(received), dim=-1), o_weight)
 
 
 def placement(topo: Topology, rank: int):

@@ -97,6 +97,71 @@ class EmulatedGroup:
         self.status.free()
 
 
+class EmulatedOprojGroup:
+    """The inverse exchange + output projection for the ranks of one SP group
+    on one GPU.  A real group runs one launch per rank; here the ranks' kernels
+    must not wait for one another, so each call runs in two phases: every
+    rank's push (FU_OPROJ_GATHER_ONLY), then every rank's GEMM
+    (FU_OPROJ_GEMM_ONLY)."""
+
+    def __init__(self, *, sp_size, hidden_size, q_heads, max_local_tokens, device="cuda",
+                 timeout_s=2.0):
+        """``q_heads`` is the local (post base-TP) query head count."""
+        self.S = sp_size
+        self.H = hidden_size
+        self.q_heads = q_heads
+        self.max_local_tokens = max_local_tokens
+        self.device = torch.device(device)
+        words = _C.oproj_sync_words(max_local_tokens)
+        self.gather = [torch.full((max_local_tokens, q_heads * HEAD), float("nan"),
+                                  dtype=torch.bfloat16, device=self.device)
+                       for _ in range(sp_size)]
+        self.sync = [torch.zeros(words, dtype=torch.int32, device=self.device)
+                     for _ in range(sp_size)]
+        self.status = _C.StatusWord()
+        self.ops = []
+        for r in range(sp_size):
+            t = _C.OprojTopology()
+            t.device = self.device.index or 0
+            t.sp_size = sp_size
+            t.sp_rank = r
+            t.q_heads = q_heads
+            t.hidden_size = hidden_size
+            t.max_local_tokens = max_local_tokens
+            for d in range(sp_size):
+                t.gather[d] = self.gather[d].data_ptr()
+                t.sync[d] = self.sync[d].data_ptr()
+            t.status = self.status.device_ptr
+            t.status_host = self.status.host_ptr
+            t.timeout_ns = int(timeout_s * 1e9)
+            self.ops.append(_C.OprojOp(t))
+
+    def run(self, attn_outs, weights, outs, tokens):
+        stream = _C.current_stream_handle(self.device.index or 0)
+        base = _C.FU_FWD_NO_PEER_WAIT
+        for r in range(self.S):
+            self.ops[r].forward(attn_outs[r].data_ptr(), None, tokens, None,
+                                base | _C.FU_OPROJ_GATHER_ONLY, stream)
+        for r in range(self.S):
+            self.ops[r].forward(attn_outs[r].data_ptr(), weights[r].data_ptr(), tokens,
+                                outs[r].data_ptr(), base | _C.FU_OPROJ_GEMM_ONLY, stream)
+
+    def counters_reset(self):
+        """Completion, work and ready counters are back at zero after a call."""
+        for block in self.sync:
+            b = block.cpu()
+            if int(b[_C.FU_SYNC_COUNTER]) or int(b[_C.FU_SYNC_EPOCH + 1]):
+                return False
+            if bool((b[_C.FU_OPROJ_READY:] != 0).any()):
+                return False
+        return True
+
+    def close(self):
+        for op in self.ops:
+            op.destroy()
+        self.status.free()
+
+
 def to_device(params, device):
     out = {}
     for k, v in params.items():

@@ -56,13 +56,41 @@ def test_constants_match_header():
         assert m and int(m.group(1)) == getattr(_C, name), name
 
 
+def test_oproj_constants_and_errors_without_gpu():
+    text = HEADER.read_text()
+    assert re.search(r"#define FU_OPROJ_READY FU_SYNC_WORDS", text)
+    assert _C.FU_OPROJ_READY == _C.FU_SYNC_WORDS
+    for name, bit in (("FU_OPROJ_GATHER_ONLY", 20), ("FU_OPROJ_GEMM_ONLY", 21)):
+        assert re.search(rf"#define {name} \(1u << {bit}\)", text), name
+        assert getattr(_C, name) == 1 << bit
+    # 64 words of flags and counters, then one ready counter per 128-row m-block.
+    assert _C.oproj_sync_words(1) == _C.FU_SYNC_WORDS + 1
+    assert _C.oproj_sync_words(4096) == _C.FU_SYNC_WORDS + 32
+    assert _C.oproj_sync_words(0) == 0
+    handle = ctypes.c_void_p()
+    assert _C.lib.fu_oproj_create(None, ctypes.byref(handle)) == _C.FU_ERR_INVALID
+    t = _C.OprojTopology()
+    t.sp_size, t.sp_rank, t.q_heads, t.hidden_size, t.max_local_tokens = 2, 0, 5, 512, 8
+    assert _C.lib.fu_oproj_create(ctypes.byref(t), ctypes.byref(handle)) == _C.FU_ERR_INVALID
+    assert "multiple of 2" in _C.last_error()
+    t.q_heads, t.hidden_size = 4, 320
+    assert _C.lib.fu_oproj_create(ctypes.byref(t), ctypes.byref(handle)) == _C.FU_ERR_INVALID
+    assert "hidden_size" in _C.last_error()
+    t.hidden_size = 512
+    assert _C.lib.fu_oproj_create(ctypes.byref(t), ctypes.byref(handle)) == _C.FU_ERR_INVALID
+    assert "missing buffer" in _C.last_error()
+
+
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="no host C compiler")
-def test_topology_struct_layout(tmp_path):
-    fields = [f[0] for f in _C.Topology._fields_]
+@pytest.mark.parametrize("cname,struct", [("fu_qkv_topology", "Topology"),
+                                          ("fu_oproj_topology", "OprojTopology")])
+def test_topology_struct_layout(tmp_path, cname, struct):
+    py = getattr(_C, struct)
+    fields = [f[0] for f in py._fields_]
     src = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"',
-           "int main(void) {", 'printf("size %zu\\n", sizeof(fu_qkv_topology));']
+           "int main(void) {", f'printf("size %zu\\n", sizeof({cname}));']
     for f in fields:
-        src.append(f'printf("{f} %zu\\n", offsetof(fu_qkv_topology, {f}));')
+        src.append(f'printf("{f} %zu\\n", offsetof({cname}, {f}));')
     src += ["return 0;", "}"]
     c = tmp_path / "probe.c"
     c.write_text("\n".join(src))
@@ -71,6 +99,6 @@ def test_topology_struct_layout(tmp_path):
     out = dict(line.split() for line in subprocess.run([str(exe)], check=True,
                                                        capture_output=True,
                                                        text=True).stdout.splitlines())
-    assert int(out["size"]) == ctypes.sizeof(_C.Topology)
+    assert int(out["size"]) == ctypes.sizeof(py)
     for f in fields:
-        assert int(out[f]) == getattr(_C.Topology, f).offset, f
+        assert int(out[f]) == getattr(py, f).offset, f
