@@ -257,6 +257,77 @@ def exact_placement_case(world, sp, gloo):
     return failures
 
 
+def oproj_case(world, sp, gloo):
+    """Inverse exchange + output projection over real peer memory: calls of
+    several lengths back to back (no host rendezvous in between) and a CUDA
+    graph replayed without rendezvous, against an NCCL all_to_all of the
+    attention-output blocks followed by the FP32-accumulated projection."""
+    rank = dist.get_rank()
+    T = world // sp
+    H, heads = 4096, 32
+    topo = oracle.Topology(world, sp, heads, 8, H)
+    cols = topo.output_q_heads * oracle.HEAD_DIM
+    nccl_sp = sp_groups(world, sp, "nccl")
+    ctx = FlashUlyssesContext(rank=rank, world_size=world, max_local_tokens=4096,
+                              hidden_size=H, num_heads=heads, num_kv_heads=8, sp_size=sp,
+                              control_group=gloo, timeout_s=10.0, output_projection=True)
+    failures = []
+
+    def reference(attn, w, L):
+        send = attn.reshape(sp, L, cols).contiguous()
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=nccl_sp)
+        return oracle.o_proj(torch.cat(list(recv), dim=-1), w)
+
+    try:
+        g = torch.Generator(device="cuda").manual_seed(100 + rank // sp)
+        w = (torch.randn(H, topo.local_q_heads * oracle.HEAD_DIM, device="cuda", generator=g)
+             * (topo.local_q_heads * oracle.HEAD_DIM) ** -0.5).bfloat16()
+        gx = torch.Generator(device="cuda").manual_seed(200 + rank)
+        lengths = (1, 129, 1024, 4096)
+        attns = [torch.randn(sp * L, cols, device="cuda", generator=gx).bfloat16()
+                 for L in lengths]
+        wants = [reference(a, w, L) for a, L in zip(attns, lengths)]
+        torch.cuda.synchronize()
+        dist.barrier(group=gloo)
+        outs = [ctx.ulysses_o_proj_forward(a, w) for a in attns]     # back to back
+        ctx.check()
+        for L, o, want in zip(lengths, outs, wants):
+            bad = int((~torch.isclose(o.float(), want.float(), atol=ATOL, rtol=RTOL)).sum())
+            if bad:
+                failures.append(f"o_proj P={world} S={sp} L={L}: {bad} violations")
+        # CUDA graph of two calls, replayed without rendezvous.
+        a, L = attns[2], lengths[2]
+        out = torch.empty(L, H, dtype=torch.bfloat16, device="cuda")
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s), torch.cuda.graph(graph, stream=s):
+            for _ in range(2):
+                ctx.ulysses_o_proj_forward(a, w, out=out)
+        torch.cuda.current_stream().wait_stream(s)
+        dist.barrier(group=gloo)
+        for _ in range(5):
+            graph.replay()
+        ctx.check()
+        bad = int((~torch.isclose(out.float(), wants[2].float(), atol=ATOL, rtol=RTOL)).sum())
+        if bad:
+            failures.append(f"o_proj graph replay P={world} S={sp}: {bad} violations")
+        epoch = int(ctx.o_barrier.data_[33].item())
+        if epoch != len(lengths) + 10:
+            failures.append(f"rank {rank}: o_proj epoch {epoch}, expected {len(lengths) + 10}")
+        if bool((ctx.o_barrier.data_[64:] != 0).any()):
+            failures.append(f"rank {rank}: ready counters not reset")
+        log(f"  o_proj P={world} S={sp} (L {lengths}, back to back, graph x5): "
+            f"{'ok' if not failures else failures}")
+        del graph
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier(group=gloo)
+        ctx.close()
+    return failures
+
+
 def fault_case(gloo):
     """A rank that never joins a call: the others' bounded wait reports it and
     the host raises, without hanging or faulting the GPU."""
@@ -311,6 +382,9 @@ def main():
         failures += exact_placement_case(world, world, gloo)
         if world >= 4:
             failures += exact_placement_case(world, world // 2, gloo)
+        failures += oproj_case(world, world, gloo)
+        if world >= 4:
+            failures += oproj_case(world, world // 2, gloo)
         failures += fault_case(gloo)
     except Exception:
         failures.append(f"rank {dist.get_rank()}: " + traceback.format_exc())
