@@ -10,18 +10,17 @@
 // (torch.nn.Linear layout).  The reference stops at the forward exchange;
 // this operator is the step its outputs feed once attention has run.
 //
-// Per CTA, 224 threads in seven warps:
+// Per CTA, 192 threads in six warps:
 //   warp 0     TMA producer: X tiles -- this rank's own heads straight from its
 //              attention output, the peers' heads from its gather buffer G
 //              once the m-block's ready counter is complete -- and W_o tiles
-//   warp 1     TMEM owner + tcgen05.mma issuer (M=128, N=256, both K-major)
-//   warps 2-5  epilogue: TMEM -> BF16 -> swizzled staging -> TMA store of out
-//   warp 6     push side of the exchange, joined by warps 2-5 until the work
-//              runs out: claims units (m-block, peer s, 32-row slice) from an
-//              atomic work counter, copies the slice's rows of this rank's
-//              attention output -- local HBM reads -- into G_s with 16-byte
-//              stores (posted NVLink writes), fences, and bumps G_s's ready
-//              counter of that m-block.
+//   warp 1     TMEM owner + tcgen05.mma issuer (M=128, N=bn, both K-major)
+//   warps 2-5  epilogue: TMEM -> BF16 -> swizzled staging -> TMA store of
+//              out.  Before it, warps 2-3 run the push side of the exchange:
+//              claims units (m-block, peer s, 8-row slice) from an atomic work
+//              counter, copies the slice's rows of this rank's attention output
+//              -- local reads -- into G_s with 16-byte posted stores (NVLink
+//              writes), fences, and bumps G_s's ready counter of that m-block.
 // Units are taken in m-block order by whichever warps are running, so no CTA
 // depends on another being resident; every wait is bounded.
 //
@@ -50,10 +49,14 @@ constexpr int BN = 256;                         // widest tile: output columns (
 constexpr int BK = 64;                          // one 128-byte swizzle row of K
 constexpr int UMMA_K = 16;
 constexpr int MAX_STAGES = 8;                   // 4 at bn = 256, 6 at 128, 8 at 64
-constexpr int NUM_THREADS = 224;
+constexpr int NUM_THREADS = 192;
 constexpr int NUM_EPI_THREADS = 128;
-constexpr int GATHER_WARP = 6;
-constexpr int SLICE_ROWS = 32;                  // rows per gather unit
+constexpr int SLICE_ROWS = 8;                   // rows per push unit
+// Epilogue warps per CTA that push first.  At 2 and 4 GPUs (L = 1024..8192)
+// two gave the best mean against NCCL all_to_all + cuBLAS: with one, the
+// push (fenced per unit) runs below the GEMM's consumption rate; with all
+// four, every m-block completes late.
+constexpr int PUSH_WARPS = 2;
 constexpr int SLICES = BM / SLICE_ROWS;
 constexpr int A_STAGE_BYTES = BM * BK * 2;      // 16 KiB, then bn * 128 bytes of W_o
 constexpr int RING_BYTES = 4 * (A_STAGE_BYTES + BN * BK * 2);   // 192 KiB
@@ -84,10 +87,10 @@ enum : int {
 struct OprojParams {
     CUtensorMap tm_g;                  // this rank's gather buffer [L, K]: box {64, 128}
     CUtensorMap tm_self;               // this rank's attention output [S * L, cpm]: box {64, 128}
-    CUtensorMap tm_w;                  // W_o [H, K]: box {64, bn}
-    CUtensorMap tm_out;                // out [L, H]: box {64, 32}
     const __nv_bfloat16* attn;         // this rank's attention output [S * L, cpm]
     __nv_bfloat16* gather[FU_MAX_SP];  // member d's gather buffer [>= L, K]
+    CUtensorMap tm_w;                  // W_o [H, K]: box {64, bn}
+    CUtensorMap tm_out;                // out [L, H]: box {64, 32}
     uint32_t* sync[FU_MAX_SP];         // member d's sync block
     int32_t* status;
     unsigned long long timeout_ns;
@@ -132,18 +135,23 @@ __device__ __forceinline__ uint32_t pack_bf16x2_rn(uint32_t lo_bits, uint32_t hi
 }
 
 // ------------------------------------------------------------ gather (push)
-// One unit: rows [row0, row0 + 32) of peer s's block of this rank's attention
-// output -> columns [me * cpm, (me + 1) * cpm) of G_s.
+// Run by PUSH_WARPS epilogue warps per CTA before their epilogue duty.  One unit: rows
+// [row0, row0 + 8) of peer s's block of this rank's attention output ->
+// columns [me * cpm, (me + 1) * cpm) of G_s: 16-byte loads from local memory,
+// 16-byte posted stores (NVLink writes for a peer), then a system-scope fence
+// and one count on G_s's ready counter of the m-block.  Small units complete
+// the first m-blocks early, while the rest of the transfer is still running.
 __device__ void run_gather(const OprojParams& p, uint32_t epoch, volatile int* abort_flag) {
     const int lane = threadIdx.x & 31;
     uint32_t* work = p.sync[p.sp_rank] + SYNC_WORK;
     const int per_m = (p.sp_size - 1) * SLICES;
     const int cpr = p.cpm / 8;                    // 16-byte chunks per row
     // i / cpr as a multiply-high: with M = floor((2^32 - 1) / cpr) + 1 the
-    // quotient is exact for i < 2^32 / cpr^2, far above a unit's 32 * cpr
+    // quotient is exact for i < 2^32 / cpr^2, far above a unit's 8 * cpr
     // chunks (cpr <= 2^13).  A 32-bit integer division per chunk (a long
     // instruction sequence on the GPU) cut a warp's copy rate by 2.5x.
     const uint32_t magic = 0xFFFFFFFFu / static_cast<uint32_t>(cpr) + 1u;
+    const int dst_row = p.K / 8;                  // 16-byte chunks per row of G
     uint32_t entered = 0;                         // members known to have entered this epoch
     while (true) {
         int u = 0;
@@ -178,7 +186,6 @@ __device__ void run_gather(const OprojParams& p, uint32_t epoch, volatile int* a
         uint4* dst = reinterpret_cast<uint4*>(p.gather[s] + static_cast<int64_t>(row0) * p.K +
                                               static_cast<int64_t>(p.sp_rank) * p.cpm);
         const int total = rows * cpr;
-        const int dst_row = p.K / 8;              // 16-byte chunks per row of G
         constexpr int U = 16;
         for (int i0 = 0; i0 < total; i0 += 32 * U) {
             uint4 v[U];
@@ -438,10 +445,12 @@ oproj_exchange_kernel(const __grid_constant__ OprojParams p) {
         if (lane == 0 && p.do_gemm) run_mma(p, smem, tmem_base, b, abort_flag);
         __syncwarp();
     } else {
-        // The gather warp and, until the units run out, the epilogue warps push
-        // rows to their owners: no tile can complete before its rows arrive.
-        if (p.do_gather) run_gather(p, epoch, abort_flag);
-        if (warp != GATHER_WARP && p.do_gemm) run_epilogue(p, smem, tmem_base, b, abort_flag);
+        // PUSH_WARPS warps per CTA push rows to their owners until the units
+        // run out, then join the epilogue.  Units are small and claimed in
+        // m-block order, so the first m-blocks -- the first wave of tiles --
+        // complete early and the tensor cores start there.
+        if (p.do_gather && warp < 2 + PUSH_WARPS) run_gather(p, epoch, abort_flag);
+        if (p.do_gemm) run_epilogue(p, smem, tmem_base, b, abort_flag);
     }
 
     tc_fence_before();
