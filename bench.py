@@ -434,46 +434,6 @@ def main():
         torch_step(i)
     torch_ms = time_steps(torch_step, min(args.steps, 20), n, group)
 
-    # The output side (no counterpart in the reference): the inverse exchange
-    # fused with the attention output projection, against NCCL all_to_all +
-    # cuBLAS on the same GPUs.
-    o_cols = ctx.output_q_heads * 128
-    o_k = ctx.local_q_heads * 128
-    og = torch.Generator(device="cuda").manual_seed(300 + rank)
-    o_sets = [(torch.randn(n * tokens, o_cols, device="cuda", generator=og).bfloat16(),
-               (torch.randn(HIDDEN, o_k, device="cuda", generator=og) * o_k ** -0.5).bfloat16())
-              for _ in range(ROTATE)]
-    o_out = torch.empty(tokens, HIDDEN, dtype=torch.bfloat16, device="cuda")
-
-    def o_step(i):
-        a, w = o_sets[i % ROTATE]
-        ctx.ulysses_o_proj_forward(a, w, out=o_out)
-
-    def o_torch_step(i):
-        a, w = o_sets[i % ROTATE]
-        if n > 1:
-            recv = torch.empty_like(a)
-            dist.all_to_all_single(recv, a)
-            a = torch.cat(list(recv.view(n, tokens, o_cols)), dim=-1)
-        torch.matmul(a, w.t(), out=o_out)
-
-    for i in range(3):
-        o_step(i)
-        o_torch_step(i)
-    o_launches0 = ctx._oproj.calls
-    o_ms = time_steps(o_step, args.steps, n, group)
-    o_launches = ctx._oproj.calls - o_launches0
-    o_torch_ms = time_steps(o_torch_step, min(args.steps, 20), n, group)
-    ctx.check()
-    o_flops = 2 * tokens * o_k * HIDDEN
-    o_proj = {"ms": round(o_ms, 5), "tflops_per_gpu": round(o_flops / (o_ms * 1e-3) / 1e12, 1),
-              "torch_nccl_cublas_ms": round(o_torch_ms, 5),
-              "speedup_vs_torch": round(o_torch_ms / o_ms, 3),
-              "nvlink_bytes_per_call": int(2 * tokens * o_k * (n - 1) / n),
-              "config": f"attn [{n * tokens}, {o_cols}] -> out [{tokens}, {HIDDEN}], "
-                        f"W_o [{HIDDEN}, {o_k}]"}
-    del o_sets
-
     sweep = {}
     if not args.no_sweep:
         for L in SWEEP:
@@ -502,6 +462,56 @@ def main():
         per, desc, threads = cpu_oracle_time(tokens, n)
         cpu = {"value": round(per, 3), "unit": "ms", "cores": threads, "kind": "port",
                "sample": desc}
+
+    # Measured last and fenced off: the headline metric above stands even if
+    # this extra measurement fails.
+    o_proj_launches = [0]
+
+    def measure_o_proj():
+        # The output side (no counterpart in the reference): the inverse exchange
+        # fused with the attention output projection, against NCCL all_to_all +
+        # cuBLAS on the same GPUs.
+        o_cols = ctx.output_q_heads * 128
+        o_k = ctx.local_q_heads * 128
+        og = torch.Generator(device="cuda").manual_seed(300 + rank)
+        o_sets = [(torch.randn(n * tokens, o_cols, device="cuda", generator=og).bfloat16(),
+                   (torch.randn(HIDDEN, o_k, device="cuda", generator=og) * o_k ** -0.5).bfloat16())
+                  for _ in range(ROTATE)]
+        o_out = torch.empty(tokens, HIDDEN, dtype=torch.bfloat16, device="cuda")
+
+        def o_step(i):
+            a, w = o_sets[i % ROTATE]
+            ctx.ulysses_o_proj_forward(a, w, out=o_out)
+
+        def o_torch_step(i):
+            a, w = o_sets[i % ROTATE]
+            if n > 1:
+                recv = torch.empty_like(a)
+                dist.all_to_all_single(recv, a)
+                a = torch.cat(list(recv.view(n, tokens, o_cols)), dim=-1)
+            torch.matmul(a, w.t(), out=o_out)
+
+        for i in range(3):
+            o_step(i)
+            o_torch_step(i)
+        o_launches0 = ctx._oproj.calls
+        o_ms = time_steps(o_step, args.steps, n, group)
+        o_proj_launches[0] = ctx._oproj.calls - o_launches0
+        o_torch_ms = time_steps(o_torch_step, min(args.steps, 20), n, group)
+        ctx.check()
+        o_flops = 2 * tokens * o_k * HIDDEN
+        return {"ms": round(o_ms, 5),
+                "tflops_per_gpu": round(o_flops / (o_ms * 1e-3) / 1e12, 1),
+                "torch_nccl_cublas_ms": round(o_torch_ms, 5),
+                "speedup_vs_torch": round(o_torch_ms / o_ms, 3),
+                "nvlink_bytes_per_call": int(2 * tokens * o_k * (n - 1) / n),
+                "config": f"attn [{n * tokens}, {o_cols}] -> out [{tokens}, {HIDDEN}], "
+                          f"W_o [{HIDDEN}, {o_k}]"}
+
+    try:
+        o_proj = measure_o_proj()
+    except Exception as e:  # reported in the JSON line instead of aborting it
+        o_proj = {"error": f"{type(e).__name__}: {e}"[:300]}
 
     traffic_map, traffic_src = profiled_traffic()
     traffic = None if not traffic_map else traffic_map.get(tokens)
@@ -538,7 +548,7 @@ def main():
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
             "o_proj": o_proj,
-            "o_proj_gpu_launches": o_launches,
+            "o_proj_gpu_launches": o_proj_launches[0],
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
