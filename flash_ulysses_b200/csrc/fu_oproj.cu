@@ -35,7 +35,6 @@
 
 #include <cstdint>
 #include <cstring>
-#include <mutex>
 
 #include "flash_ulysses_b200.h"
 #include "fu_internal.h"
@@ -479,29 +478,10 @@ oproj_exchange_kernel(const __grid_constant__ OprojParams p) {
 }  // namespace oproj
 
 // ------------------------------------------------------------ host side
-typedef CUresult (*EncodeTiledFn2)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn2 oproj_encode_fn() {
-    static EncodeTiledFn2 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        cudaDriverEntryPointQueryResult q;
-        void* ptr = nullptr;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn2>(ptr);
-    });
-    return fn;
-}
-
 // 2-D BF16 row-major [rows, cols] with a 128-byte-swizzled box {64, box_rows}.
 static int encode_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
                      uint32_t box_rows, const char* what) {
-    auto fn = oproj_encode_fn();
+    auto fn = encode_tiled_fn();
     if (fn == nullptr) return set_error(FU_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
