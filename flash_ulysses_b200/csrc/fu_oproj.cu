@@ -50,13 +50,12 @@ constexpr int UMMA_K = 16;
 constexpr int MAX_STAGES = 8;                   // 4 at bn = 256, 6 at 128, 8 at 64
 constexpr int NUM_THREADS = 192;
 constexpr int NUM_EPI_THREADS = 128;
-constexpr int SLICE_ROWS = 8;                   // rows per push unit
+constexpr int UNIT_BYTES = 32 * 1024;           // target bytes of one push unit
 // Epilogue warps per CTA that push first.  At 2 and 4 GPUs (L = 1024..8192)
 // two gave the best mean against NCCL all_to_all + cuBLAS: with one, the
 // push (fenced per unit) runs below the GEMM's consumption rate; with all
 // four, every m-block completes late.
 constexpr int PUSH_WARPS = 2;
-constexpr int SLICES = BM / SLICE_ROWS;
 constexpr int A_STAGE_BYTES = BM * BK * 2;      // 16 KiB, then bn * 128 bytes of W_o
 constexpr int RING_BYTES = 4 * (A_STAGE_BYTES + BN * BK * 2);   // 192 KiB
 constexpr int OFF_RING = 0;
@@ -97,6 +96,7 @@ struct OprojParams {
     int32_t num_m, num_n, num_tiles, k_blocks, units;
     int32_t bn;                        // output columns per tile: 256, 128 or 64
     int32_t stages, stage_bytes;       // operand ring: RING_BYTES / stage_bytes stages
+    int32_t slice_rows, slices;        // push unit: slice_rows rows; slices = BM / slice_rows
     uint32_t wait_peers;
     uint32_t do_gather, do_gemm;       // both in one call; one each in the two-phase mode
 };
@@ -134,8 +134,9 @@ __device__ __forceinline__ uint32_t pack_bf16x2_rn(uint32_t lo_bits, uint32_t hi
 }
 
 // ------------------------------------------------------------ gather (push)
-// Run by PUSH_WARPS epilogue warps per CTA before their epilogue duty.  One unit: rows
-// [row0, row0 + 8) of peer s's block of this rank's attention output ->
+// Run by PUSH_WARPS epilogue warps per CTA before their epilogue duty.  One unit:
+// rows [row0, row0 + slice_rows) (~32 KiB) of peer s's block of this rank's
+// attention output ->
 // columns [me * cpm, (me + 1) * cpm) of G_s: 16-byte loads from local memory,
 // 16-byte posted stores (NVLink writes for a peer), then a system-scope fence
 // and one count on G_s's ready counter of the m-block.  Small units complete
@@ -143,12 +144,12 @@ __device__ __forceinline__ uint32_t pack_bf16x2_rn(uint32_t lo_bits, uint32_t hi
 __device__ void run_gather(const OprojParams& p, uint32_t epoch, volatile int* abort_flag) {
     const int lane = threadIdx.x & 31;
     uint32_t* work = p.sync[p.sp_rank] + SYNC_WORK;
-    const int per_m = (p.sp_size - 1) * SLICES;
+    const int per_m = (p.sp_size - 1) * p.slices;
     const int cpr = p.cpm / 8;                    // 16-byte chunks per row
     // i / cpr as a multiply-high: with M = floor((2^32 - 1) / cpr) + 1 the
-    // quotient is exact for i < 2^32 / cpr^2, far above a unit's 8 * cpr
-    // chunks (cpr <= 2^13).  A 32-bit integer division per chunk (a long
-    // instruction sequence on the GPU) cut a warp's copy rate by 2.5x.
+    // quotient is exact for i < 2^32 / cpr, far above a unit's slice_rows * cpr
+    // chunks.  A 32-bit integer division per chunk (a long instruction
+    // sequence on the GPU) cut a warp's copy rate by 2.5x.
     const uint32_t magic = 0xFFFFFFFFu / static_cast<uint32_t>(cpr) + 1u;
     const int dst_row = p.K / 8;                  // 16-byte chunks per row of G
     uint32_t entered = 0;                         // members known to have entered this epoch
@@ -159,10 +160,10 @@ __device__ void run_gather(const OprojParams& p, uint32_t epoch, volatile int* a
         if (u >= p.units || *abort_flag) break;
         const int mb = u / per_m;
         const int rest = u - mb * per_m;
-        const int sv = rest / SLICES;                 // peers only: this rank's own
+        const int sv = rest / p.slices;               // peers only: this rank's own
         const int s = sv + (sv >= p.sp_rank ? 1 : 0); // columns are read in place
-        const int row0 = mb * BM + (rest - sv * SLICES) * SLICE_ROWS;
-        const int rows = max(0, min(SLICE_ROWS, p.L - row0));
+        const int row0 = mb * BM + (rest - sv * p.slices) * p.slice_rows;
+        const int rows = max(0, min(p.slice_rows, p.L - row0));
         // G_s must no longer be read by s's previous call: wait until s entered.
         if (p.wait_peers && !(entered & (1u << s))) {
             if (lane == 0) {
@@ -216,7 +217,7 @@ __device__ void run_producer(const OprojParams& p, uint8_t* smem, const Bars& b,
                              volatile int* abort_flag) {
     const uint32_t ring = smem_u32(smem + OFF_RING);
     const uint32_t* ready = p.sync[p.sp_rank] + FU_OPROJ_READY;
-    const uint32_t target = static_cast<uint32_t>((p.sp_size - 1) * SLICES);
+    const uint32_t target = static_cast<uint32_t>((p.sp_size - 1) * p.slices);
     // K-blocks of this rank's own heads come straight from its attention output.
     const int self_kb0 = p.sp_rank * p.cpm / BK;
     const int self_kb1 = self_kb0 + p.cpm / BK;
@@ -635,7 +636,12 @@ extern "C" int fu_oproj_forward(fu_oproj_ctx* ctx, const void* attn, const void*
     p.num_n = static_cast<int32_t>(H / bn);
     p.num_tiles = do_gemm ? p.num_m * p.num_n : 0;
     p.k_blocks = static_cast<int32_t>(K / oproj::BK);
-    p.units = do_gather ? p.num_m * (S - 1) * oproj::SLICES : 0;
+    // Push units of ~32 KiB: 8 to 128 rows (a power of two) of cpm columns.
+    int slice_rows = 8;
+    while (slice_rows < oproj::BM && 2 * slice_rows * cpm * 2 <= oproj::UNIT_BYTES) slice_rows *= 2;
+    p.slice_rows = slice_rows;
+    p.slices = oproj::BM / slice_rows;
+    p.units = do_gather ? p.num_m * (S - 1) * p.slices : 0;
     p.wait_peers = (flags & FU_FWD_NO_PEER_WAIT) == 0 ? 1u : 0u;
     p.do_gather = do_gather ? 1u : 0u;
     p.do_gemm = do_gemm ? 1u : 0u;
