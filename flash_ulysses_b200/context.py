@@ -240,6 +240,19 @@ class FlashUlyssesContext:
         local_tokens = rows // self.sp_size
         if not 0 < local_tokens <= self.max_local_tokens:
             raise ValueError("Input length must be within [1, max_local_tokens]")
+        # The kernel's tensor maps are built from these shapes, so a tensor of
+        # another shape, dtype or layout would be read or written out of bounds.
+        k = self.local_q_heads * self.head_dim
+        for name, t, shape in (
+                ("attn_output", attn_output, (rows, self.output_q_heads * self.head_dim)),
+                ("o_proj_weight", o_proj_weight, (self.hidden_size, k)),
+                ("out", out, (local_tokens, self.hidden_size))):
+            if t is None:
+                continue
+            if (tuple(t.shape) != shape or t.dtype != torch.bfloat16 or not t.is_contiguous()
+                    or t.device != self.device):
+                raise ValueError(f"{name} must be a contiguous BF16 tensor of shape {shape} "
+                                 f"on {self.device}")
         if self._status.value:
             raise RuntimeError("an earlier call failed on the device: "
                                + _C.decode_status(self._status.value))

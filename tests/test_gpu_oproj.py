@@ -159,3 +159,25 @@ def test_context_requires_output_projection():
                                        torch.zeros(512, 512, dtype=torch.bfloat16, device="cuda"))
     finally:
         ctx.close()
+
+
+def test_context_rejects_bad_shapes():
+    from flash_ulysses_b200 import FlashUlyssesContext
+    ctx = FlashUlyssesContext(rank=0, world_size=1, max_local_tokens=16, hidden_size=512,
+                              num_heads=4, num_kv_heads=2, sp_size=1, output_projection=True)
+    try:
+        bf = dict(dtype=torch.bfloat16, device="cuda")
+        attn = torch.zeros(16, 512, **bf)
+        w = torch.zeros(512, 512, **bf)
+        for a, ww, o in ((torch.zeros(16, 384, **bf), w, None),
+                         (attn, torch.zeros(512, 256, **bf), None),
+                         (attn.float(), w, None),
+                         (attn, w.t(), None),
+                         (attn, w, torch.zeros(8, 512, **bf)),
+                         (torch.zeros(17, 512, **bf), w, None)):
+            with pytest.raises(ValueError):
+                ctx.ulysses_o_proj_forward(a, ww, out=o)
+        ctx.ulysses_o_proj_forward(attn, w)
+        ctx.check()
+    finally:
+        ctx.close()
