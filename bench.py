@@ -400,29 +400,64 @@ def main():
     # The reference harness's per-call method (rendezvous between calls).
     iso = time_isolated(step, min(args.steps, 20), n, group)
 
-    # e2e: through the public API from pinned host memory, outputs read back.
+    # e2e: through the public API from pinned host memory, every step's inputs
+    # uploaded and its Q/K/V read back inside the timed region.  Uploads run on
+    # their own stream into double-buffered inputs and read-backs on another,
+    # so step i's read-back overlaps step i+1's upload on the two copy engines;
+    # a call waits for the previous read-back because its outputs alias the
+    # receive buffers.
     hx = [s[0].cpu().pin_memory() for s in sets]
     hp = [s[1].cpu().pin_memory() for s in sets]
-    dx = torch.empty_like(sets[0][0])
-    dp = torch.empty_like(sets[0][1])
+    dx = [torch.empty_like(sets[0][0]) for _ in range(2)]
+    dp = [torch.empty_like(sets[0][1]) for _ in range(2)]
     outs_h = [torch.empty((tokens * n, w), dtype=torch.bfloat16).pin_memory()
               for w in (ctx.output_q_heads * 128, ctx.output_kv_heads * 128,
                         ctx.output_kv_heads * 128)]
+    main_stream = torch.cuda.current_stream()
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    in_free = [torch.cuda.Event() for _ in range(2)]
+    computed, read_back = torch.cuda.Event(), torch.cuda.Event()
 
     def e2e_step(i):
+        b = i % 2
         _, _, p = sets[i % ROTATE]
-        dx.copy_(hx[i % ROTATE], non_blocking=True)
-        dp.copy_(hp[i % ROTATE], non_blocking=True)
-        q, k, v = ctx.ulysses_qkv_forward(dx, p["qkv_weight"], dp, p["q_norm_weight"],
+        up.wait_event(in_free[b])                 # the call of step i-2 consumed dx[b]
+        with torch.cuda.stream(up):
+            dx[b].copy_(hx[i % ROTATE], non_blocking=True)
+            dp[b].copy_(hp[i % ROTATE], non_blocking=True)
+        in_ready[b].record(up)
+        main_stream.wait_event(in_ready[b])
+        main_stream.wait_event(read_back)         # outputs alias the receive buffers
+        q, k, v = ctx.ulysses_qkv_forward(dx[b], p["qkv_weight"], dp[b], p["q_norm_weight"],
                                           p["k_norm_weight"], p["rope_cache"],
                                           q_epsilon=p["q_epsilon"], k_epsilon=p["k_epsilon"])
-        for h, d in zip(outs_h, (q, k, v)):
-            h.copy_(d, non_blocking=True)
+        in_free[b].record(main_stream)
+        computed.record(main_stream)
+        down.wait_event(computed)
+        with torch.cuda.stream(down):
+            for h, d in zip(outs_h, (q, k, v)):
+                h.copy_(d, non_blocking=True)
+        read_back.record(down)
+
+    def time_e2e(steps):
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        rendezvous(n, group)
+        start.record()
+        up.wait_stream(main_stream)
+        for i in range(steps):
+            e2e_step(i)
+        main_stream.wait_event(read_back)         # the last read-back is inside the region
+        end.record()
+        rendezvous(n, group)
+        return max_over_ranks(start.elapsed_time(end) / steps, n)
 
     for i in range(2):
         e2e_step(i)
-    e2e_ms = time_steps(e2e_step, args.steps, n, group)
-    h2d = dx.numel() * 2 + dp.numel() * 8
+    torch.cuda.synchronize()
+    e2e_ms = time_e2e(args.steps)
+    h2d = dx[0].numel() * 2 + dp[0].numel() * 8
     d2h = sum(t.numel() * 2 for t in outs_h)
 
     # The reference's own PyTorch + NCCL path on the same GPUs.
