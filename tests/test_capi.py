@@ -102,3 +102,36 @@ def test_topology_struct_layout(tmp_path, cname, struct):
     assert int(out["size"]) == ctypes.sizeof(py)
     for f in fields:
         assert int(out[f]) == getattr(py, f).offset, f
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="no host C compiler")
+def test_c_caller_links_and_calls_the_abi(tmp_path):
+    """A plain C program includes the header, links the library and calls the
+    entry points that need no GPU: version, argument checking and its error
+    channel, sizes."""
+    src = tmp_path / "caller.c"
+    src.write_text(f"""
+#include <stdio.h>
+#include <string.h>
+#include "{HEADER}"
+int main(void) {{
+    fu_qkv_ctx* q = NULL;
+    fu_oproj_ctx* o = NULL;
+    if (fu_version() < 1) return 1;
+    if (fu_qkv_create(NULL, &q) != FU_ERR_INVALID || q != NULL) return 2;
+    if (strstr(fu_last_error(), "null") == NULL) return 3;
+    if (fu_oproj_create(NULL, &o) != FU_ERR_INVALID) return 4;
+    if (fu_oproj_sync_words(4096) != FU_OPROJ_READY + 32) return 5;
+    if (fu_qkv_forward(NULL, NULL, NULL, NULL, NULL, NULL, NULL, 1, 1, 1e-6, 1e-6, 0,
+                       NULL, NULL) != FU_ERR_INVALID) return 6;
+    printf("ok %d\\n", fu_version());
+    return 0;
+}}
+""")
+    exe = tmp_path / "caller"
+    lib_dir = str(_C.LIB_PATH.parent)
+    subprocess.run(["gcc", "-std=c11", str(src), "-L", lib_dir, f"-l:{_C.LIB_PATH.name}",
+                    f"-Wl,-rpath,{lib_dir}", "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert out.returncode == 0, (out.returncode, out.stderr)
+    assert out.stdout.startswith("ok ")
