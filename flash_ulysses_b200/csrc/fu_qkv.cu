@@ -830,8 +830,32 @@ __device__ __forceinline__ void split_item_load(const QkvParams& p, uint32_t loc
         }
 }
 
+// cos|sin of columns 4l..4l+3 (mod 64) at token row m's position, for a Q/K
+// head (V heads are not rotated); issued before the partial sums are read so
+// the two latencies overlap.
+struct SplitRope {
+    float4 cs, sn;
+};
+
+__device__ __forceinline__ SplitRope split_item_rope(const QkvParams& p, int m, int h, int lane) {
+    SplitRope r;
+    r.cs = r.sn = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (h < p.q_heads + p.kv_heads) {
+        int64_t pos = __ldg(p.positions + m);
+        if (pos < 0 || pos >= p.rope_rows) {
+            report_status(p.status, FU_DEV_POSITION_RANGE, 0);
+            pos = 0;
+        }
+        const int j0 = 4 * (lane & 15);
+        r.cs = __ldg(reinterpret_cast<const float4*>(p.rope + pos * 128 + j0));
+        r.sn = __ldg(reinterpret_cast<const float4*>(p.rope + pos * 128 + 64 + j0));
+    }
+    return r;
+}
+
 __device__ __forceinline__ void split_item_emit(const QkvParams& p, const float4& acc, int m,
-                                                int h, const float* gam, int lane) {
+                                                int h, const float* gam, int lane,
+                                                const SplitRope& rope) {
     // BF16 projection of columns 4l..4l+3 of head h, token row m.
     const uint32_t u0 = pack_bf16x2(acc.x, acc.y);
     const uint32_t u1 = pack_bf16x2(acc.z, acc.w);
@@ -871,16 +895,8 @@ __device__ __forceinline__ void split_item_emit(const QkvParams& p, const float4
         for (int i = 0; i < 4; ++i) n[i] = round_if(__fmul_rn(__fmul_rn(v[i], scale), g[i]), r16);
 #pragma unroll
         for (int i = 0; i < 4; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, n[i], 16);
-        int64_t pos = __ldg(p.positions + m);
-        if (pos < 0 || pos >= p.rope_rows) {
-            report_status(p.status, FU_DEV_POSITION_RANGE, 0);
-            pos = 0;
-        }
-        const int j0 = 4 * (lane & 15);
-        const float4 cs = __ldg(reinterpret_cast<const float4*>(p.rope + pos * 128 + j0));
-        const float4 sn = __ldg(reinterpret_cast<const float4*>(p.rope + pos * 128 + 64 + j0));
-        const float c4[4] = {cs.x, cs.y, cs.z, cs.w};
-        const float s4[4] = {sn.x, sn.y, sn.z, sn.w};
+        const float c4[4] = {rope.cs.x, rope.cs.y, rope.cs.z, rope.cs.w};
+        const float s4[4] = {rope.sn.x, rope.sn.y, rope.sn.z, rope.sn.w};
         float r[4];
         if (lane < 16) {        // lo half: lo*cos - hi*sin
 #pragma unroll
@@ -917,11 +933,13 @@ __device__ void run_split_reduce(const QkvParams& p, const Sched& sc, uint8_t* s
         const bool has1 = i1 < items;
         const int r0 = i0 / heads_here, hs0 = i0 % heads_here;
         const int r1 = has1 ? i1 / heads_here : r0, hs1 = has1 ? i1 % heads_here : hs0;
+        const SplitRope rope0 = split_item_rope(p, m_blk * BM + r0, n_blk * 2 + hs0, lane);
+        const SplitRope rope1 = split_item_rope(p, m_blk * BM + r1, n_blk * 2 + hs1, lane);
         float4 a0, a1;
         split_item_load(p, part + r0 * PART_STRIDE + (hs0 * 128 + 4 * lane) * 4, p.splits, a0);
         split_item_load(p, part + r1 * PART_STRIDE + (hs1 * 128 + 4 * lane) * 4, p.splits, a1);
-        split_item_emit(p, a0, m_blk * BM + r0, n_blk * 2 + hs0, gam, lane);
-        if (has1) split_item_emit(p, a1, m_blk * BM + r1, n_blk * 2 + hs1, gam, lane);
+        split_item_emit(p, a0, m_blk * BM + r0, n_blk * 2 + hs0, gam, lane, rope0);
+        if (has1) split_item_emit(p, a1, m_blk * BM + r1, n_blk * 2 + hs1, gam, lane, rope1);
     }
 }
 
