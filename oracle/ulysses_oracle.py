@@ -246,7 +246,7 @@ def placement(topo: Topology, rank: int):
 
     Returns a list, indexed by local packed head, of
     ``(component, dst_rank, dst_head_column)`` following the reference's
-    mapping (DESIGN.md:28-37, flash_ulysses_kernel_hopper.cu:211-218).
+    mapping (the reference's DESIGN.md:28-37, flash_ulysses_kernel_hopper.cu:211-218).
     """
     start = rank // topo.sp_size * topo.sp_size
     out = []
