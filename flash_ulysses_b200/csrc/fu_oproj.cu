@@ -212,24 +212,47 @@ __device__ void run_gather(const OprojParams& p, uint32_t epoch, volatile int* a
     }
 }
 
+// ------------------------------------------------------------ schedule
+// Tiles of 128 (single CTA) or 256 rows (CTA pair, tcgen05 cta_group::2: each
+// CTA loads its own 128 rows of X and half of the W_o tile's rows, the leader
+// issues M=256 MMAs, each CTA drains its own TMEM lanes) by bn columns,
+// persistent over the grid's CTAs or pairs.
+template <bool kPair>
+struct Sched {
+    int first, stride, rank;
+    __device__ Sched() {
+        rank = kPair ? static_cast<int>(cluster_ctarank()) : 0;
+        first = kPair ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
+        stride = kPair ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
+    }
+    // This CTA's 128-row m-block of tile t.
+    __device__ int m_block(const OprojParams& p, int t) const {
+        const int mt = t / p.num_n;
+        return kPair ? 2 * mt + rank : mt;
+    }
+};
+
 // ------------------------------------------------------------ producer
+template <bool kPair>
 __device__ void run_producer(const OprojParams& p, uint8_t* smem, const Bars& b,
                              volatile int* abort_flag) {
+    const Sched<kPair> sc;
     const uint32_t ring = smem_u32(smem + OFF_RING);
     const uint32_t* ready = p.sync[p.sp_rank] + FU_OPROJ_READY;
     const uint32_t target = static_cast<uint32_t>((p.sp_size - 1) * p.slices);
     // K-blocks of this rank's own heads come straight from its attention output.
     const int self_kb0 = p.sp_rank * p.cpm / BK;
     const int self_kb1 = self_kb0 + p.cpm / BK;
+    const int b_rows = kPair ? p.bn / 2 : p.bn;   // W_o rows this CTA loads per tile
     int stage = 0;
     uint32_t phase = 0;
     uint32_t issued_mask = 0, last_parity = 0;
     int ready_m = -1;                             // highest m-block known complete
     bool ok = true;
-    for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
-        const int mb = t / p.num_n;
-        const int nb = t - mb * p.num_n;
-        if (mb > ready_m && target > 0) {
+    for (int t = sc.first; ok && t < p.num_tiles; t += sc.stride) {
+        const int mb = sc.m_block(p, t);
+        const int nb = t % p.num_n;
+        if (mb > ready_m && target > 0 && mb < p.num_m) {
             // Every source's slices of this m-block have landed in G.
             const uint64_t t0 = globaltimer_ns();
             while (ld_acquire_sys_u32(ready + mb) < target) {
@@ -251,15 +274,29 @@ __device__ void run_producer(const OprojParams& p, uint8_t* smem, const Bars& b,
                 ok = false;
                 break;
             }
-            const uint32_t full = b.full + 8 * stage;
             const uint32_t adst = ring + stage * p.stage_bytes;
-            mbar_arrive_expect_tx(full, p.stage_bytes);
-            if (kb >= self_kb0 && kb < self_kb1)
-                tma_load_2d(adst, &p.tm_self, full, (kb - self_kb0) * BK,
-                            p.sp_rank * p.L + mb * BM);
-            else
-                tma_load_2d(adst, &p.tm_g, full, kb * BK, mb * BM);
-            tma_load_2d(adst + A_STAGE_BYTES, &p.tm_w, full, kb * BK, nb * p.bn);
+            const int ka = kb >= self_kb0 && kb < self_kb1;
+            if (kPair) {
+                // Both CTAs' bytes are counted on the leader's barrier.
+                const uint32_t full = map_cluster_smem(b.full + 8 * stage, 0);
+                if (sc.rank == 0) mbar_arrive_expect_tx(b.full + 8 * stage, 2 * p.stage_bytes);
+                if (ka)
+                    tma_load_2d_pair(adst, &p.tm_self, full, (kb - self_kb0) * BK,
+                                     p.sp_rank * p.L + mb * BM);
+                else
+                    tma_load_2d_pair(adst, &p.tm_g, full, kb * BK, mb * BM);
+                tma_load_2d_pair(adst + A_STAGE_BYTES, &p.tm_w, full, kb * BK,
+                                 nb * p.bn + sc.rank * b_rows);
+            } else {
+                const uint32_t full = b.full + 8 * stage;
+                mbar_arrive_expect_tx(full, p.stage_bytes);
+                if (ka)
+                    tma_load_2d(adst, &p.tm_self, full, (kb - self_kb0) * BK,
+                                p.sp_rank * p.L + mb * BM);
+                else
+                    tma_load_2d(adst, &p.tm_g, full, kb * BK, mb * BM);
+                tma_load_2d(adst + A_STAGE_BYTES, &p.tm_w, full, kb * BK, nb * p.bn);
+            }
             issued_mask |= 1u << stage;
             last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
             if (++stage == p.stages) {
@@ -269,24 +306,35 @@ __device__ void run_producer(const OprojParams& p, uint8_t* smem, const Bars& b,
         }
     }
     if (!ok) {
-        // Loads already issued must land before shared memory is released.
-        for (int s = 0; s < p.stages; ++s)
-            if (issued_mask & (1u << s))
-                drain_wait(b.full + 8 * s, (last_parity >> s) & 1u, p.timeout_ns, p.status);
+        if (kPair) {
+            // This CTA's loads are counted on the leader's barriers; give any
+            // still in flight time to land before shared memory is released.
+            const uint64_t t0 = globaltimer_ns();
+            while (globaltimer_ns() - t0 < 100000) {
+            }
+        } else {
+            // Loads already issued must land before shared memory is released.
+            for (int s = 0; s < p.stages; ++s)
+                if (issued_mask & (1u << s))
+                    drain_wait(b.full + 8 * s, (last_parity >> s) & 1u, p.timeout_ns, p.status);
+        }
     }
 }
 
 // ------------------------------------------------------------ MMA
+// Single CTA, or the pair's leader only.
+template <bool kPair>
 __device__ void run_mma(const OprojParams& p, uint8_t* smem, uint32_t tmem_base, const Bars& b,
                         volatile int* abort_flag) {
-    const uint32_t idesc = make_idesc_bf16_f32(BM, p.bn, /*a_mn_major=*/false,
+    const Sched<kPair> sc;
+    const uint32_t idesc = make_idesc_bf16_f32(kPair ? 2 * BM : BM, p.bn, /*a_mn_major=*/false,
                                                /*b_mn_major=*/false);
     const uint32_t ring = smem_u32(smem + OFF_RING);
     int stage = 0;
     uint32_t phase = 0;
     int local = 0;
     bool ok = true;
-    for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x, ++local) {
+    for (int t = sc.first; ok && t < p.num_tiles; t += sc.stride, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!fu_wait_parity(b.tempty + 8 * acc, acc_phase ^ 1u, abort_flag, p.timeout_ns,
@@ -308,26 +356,47 @@ __device__ void run_mma(const OprojParams& p, uint8_t* smem, uint32_t tmem_base,
 #pragma unroll
             for (int k = 0; k < BK / UMMA_K; ++k) {
                 // Both operands K-major with 128-byte swizzle: K advances 32 bytes
-                // inside the swizzle row; 8-row groups are 1024 bytes apart.
+                // inside the swizzle row; 8-row groups are 1024 bytes apart.  In a
+                // pair each CTA holds its own A rows and half of B's rows at the
+                // same offsets.
                 const uint64_t adesc = make_smem_desc_sw128(a_base + k * UMMA_K * 2, 16, 1024);
                 const uint64_t bdesc = make_smem_desc_sw128(b_base + k * UMMA_K * 2, 16, 1024);
-                tc_mma_bf16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+                const uint32_t accum = (kb | k) != 0 ? 1u : 0u;
+                if (kPair)
+                    tc_mma_bf16_pair(d_tmem, adesc, bdesc, idesc, accum);
+                else
+                    tc_mma_bf16(d_tmem, adesc, bdesc, idesc, accum);
             }
-            tc_commit(b.empty + 8 * stage);
+            // Frees the stage (in both CTAs of a pair) when these MMAs finish.
+            if (kPair)
+                tc_commit_pair_mc(b.empty + 8 * stage, 0x3);
+            else
+                tc_commit(b.empty + 8 * stage);
             if (++stage == p.stages) {
                 stage = 0;
                 phase ^= 1u;
             }
         }
-        if (ok) tc_commit(b.tfull + 8 * acc);
+        if (ok) {
+            if (kPair)
+                tc_commit_pair_mc(b.tfull + 8 * acc, 0x3);
+            else
+                tc_commit(b.tfull + 8 * acc);
+        }
     }
-    tc_commit(b.mma_done);
+    // Every MMA this thread issued must finish before TMEM is released.
+    if (kPair)
+        tc_commit_pair_mc(b.mma_done, 0x1);
+    else
+        tc_commit(b.mma_done);
     drain_wait(b.mma_done, 0, p.timeout_ns, p.status);
 }
 
 // ------------------------------------------------------------ epilogue
+template <bool kPair>
 __device__ void run_epilogue(const OprojParams& p, uint8_t* smem, uint32_t tmem_base,
                              const Bars& b, volatile int* abort_flag) {
+    const Sched<kPair> sc;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int quarter = warp & 3;                 // TMEM lanes this warp may access
@@ -336,11 +405,11 @@ __device__ void run_epilogue(const OprojParams& p, uint8_t* smem, uint32_t tmem_
     const uint32_t swz_row = lane * 128;
     const int swz = lane & 7;
     int local = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+    for (int t = sc.first; t < p.num_tiles; t += sc.stride, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        const int mb = t / p.num_n;
-        const int nb = t - mb * p.num_n;
+        const int mb = sc.m_block(p, t);
+        const int nb = t % p.num_n;
         if (!fu_wait_parity(b.tfull + 8 * acc, acc_phase, abort_flag, p.timeout_ns, p.status,
                             W_TFULL))
             break;
@@ -385,14 +454,20 @@ __device__ void run_epilogue(const OprojParams& p, uint8_t* smem, uint32_t tmem_
                 bulk_commit_group();
             }
         }
+        // The accumulator has been read: hand TMEM back (to the pair leader's
+        // MMA issuer, which counts both CTAs' threads).
         tc_fence_before();
-        mbar_arrive(b.tempty + 8 * acc);
+        if (kPair && sc.rank != 0)
+            mbar_arrive_remote(map_cluster_smem(b.tempty + 8 * acc, 0));
+        else
+            mbar_arrive(b.tempty + 8 * acc);
     }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
 }
 
 // ------------------------------------------------------------ kernel
+template <bool kPair>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 oproj_exchange_kernel(const __grid_constant__ OprojParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -405,6 +480,7 @@ oproj_exchange_kernel(const __grid_constant__ OprojParams p) {
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
     uint32_t* epoch_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC + 8);
     uint32_t* my_sync = p.sync[p.sp_rank];
+    const bool leader = !kPair || cluster_ctarank() == 0;
 
     if (threadIdx.x == 0) {
         const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my_sync + FU_SYNC_EPOCH) + 1;
@@ -418,7 +494,8 @@ oproj_exchange_kernel(const __grid_constant__ OprojParams p) {
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(b.tfull + 8 * a, 1);
-            mbar_init(b.tempty + 8 * a, NUM_EPI_THREADS);
+            // A pair's leader counts the epilogue threads of both CTAs.
+            mbar_init(b.tempty + 8 * a, kPair ? 2 * NUM_EPI_THREADS : NUM_EPI_THREADS);
         }
         mbar_init(b.mma_done, 1);
         *abort_flag = 0;
@@ -429,20 +506,27 @@ oproj_exchange_kernel(const __grid_constant__ OprojParams p) {
         tma_prefetch_desc(&p.tm_out);
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
-        tmem_relinquish();
+        if (kPair) {
+            tmem_alloc_pair(smem_u32(tmem_holder), TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    // A pair's barriers and TMEM must exist in both CTAs before either uses them.
+    if (kPair) cluster_sync_all();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
     const uint32_t epoch = *epoch_slot;
 
     if (warp == 0) {
-        if (lane == 0 && p.do_gemm) run_producer(p, smem, b, abort_flag);
+        if (lane == 0 && p.do_gemm) run_producer<kPair>(p, smem, b, abort_flag);
         __syncwarp();
     } else if (warp == 1) {
-        if (lane == 0 && p.do_gemm) run_mma(p, smem, tmem_base, b, abort_flag);
+        if (lane == 0 && p.do_gemm && leader) run_mma<kPair>(p, smem, tmem_base, b, abort_flag);
         __syncwarp();
     } else {
         // PUSH_WARPS warps per CTA push rows to their owners until the units
@@ -450,13 +534,20 @@ oproj_exchange_kernel(const __grid_constant__ OprojParams p) {
         // m-block order, so the first m-blocks -- the first wave of tiles --
         // complete early and the tensor cores start there.
         if (p.do_gather && warp < 2 + PUSH_WARPS) run_gather(p, epoch, abort_flag);
-        if (p.do_gemm) run_epilogue(p, smem, tmem_base, b, abort_flag);
+        if (p.do_gemm) run_epilogue<kPair>(p, smem, tmem_base, b, abort_flag);
     }
 
     tc_fence_before();
     __syncthreads();
+    // Both CTAs of a pair are done with TMEM (reads and the leader's MMAs).
+    if (kPair) cluster_sync_all();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+    if (warp == 1) {
+        if (kPair)
+            tmem_dealloc_pair(tmem_base, TMEM_COLS);
+        else
+            tmem_dealloc(tmem_base, TMEM_COLS);
+    }
 
     // The last CTA to finish advances the epoch and resets the work counter
     // and (once this rank's tiles are done) its ready counters.
@@ -502,6 +593,7 @@ static int encode_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t c
 struct fu_oproj_ctx {
     fu_oproj_topology topo;
     int sm_count = 0;
+    int max_pairs = 0;            // co-resident CTA pairs of the pair variant
     uint32_t calls = 0;
     int last_grid = 0;
     fu::oproj::OprojParams params;
@@ -548,13 +640,36 @@ extern "C" int fu_oproj_create(const fu_oproj_topology* topo, fu_oproj_ctx** out
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(topo->device);
-    cudaError_t e = cudaFuncSetAttribute(oproj::oproj_exchange_kernel,
+    cudaError_t e = cudaFuncSetAttribute(oproj::oproj_exchange_kernel<false>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          oproj::SMEM_ALLOC);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(oproj::oproj_exchange_kernel<true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, oproj::SMEM_ALLOC);
+    int pairs = 0;
+    if (e == cudaSuccess) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * 16, 1, 1);
+        cfg.blockDim = dim3(oproj::NUM_THREADS, 1, 1);
+        cfg.dynamicSmemBytes = oproj::SMEM_ALLOC;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = 2;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&pairs, oproj::oproj_exchange_kernel<true>, &cfg) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            pairs = 0;
+        }
+    }
     cudaSetDevice(prev);
     if (e != cudaSuccess)
         return set_error(FU_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     auto* ctx = new fu_oproj_ctx();
+    ctx->max_pairs = pairs;
     ctx->topo = *topo;
     if (ctx->topo.timeout_ns == 0) ctx->topo.timeout_ns = 5000000000ull;
     ctx->sm_count = sms;
@@ -598,12 +713,19 @@ extern "C" int fu_oproj_forward(fu_oproj_ctx* ctx, const void* attn, const void*
     const int64_t K = static_cast<int64_t>(t.q_heads) * 128;
     const int cpm = t.q_heads / S * 128;
 
-    // Tile width: the widest whose tiles still cover half of the SMs (small L
-    // streams W_o through more CTAs).
+    // CTA pairs (256-row tiles) once there are two m-blocks, unless a variant
+    // is forced (FU_FWD_SINGLE / FU_FWD_PAIR).  Tile width: the widest whose
+    // tiles still cover half of the SMs or pairs (small L streams W_o through
+    // more CTAs).
     const int64_t num_m = (L + oproj::BM - 1) / oproj::BM;
+    const uint32_t variant = (flags >> 12) & 0x3u;
+    const bool pair = do_gemm && ctx->max_pairs > 0 &&
+                      (variant == 2u || (variant == 0u && num_m >= 2));
+    const int64_t row_tiles = pair ? (L + 2 * oproj::BM - 1) / (2 * oproj::BM) : num_m;
+    const int64_t slots = pair ? ctx->max_pairs : ctx->sm_count;
     int bn = 64;
     for (int c : {256, 128})
-        if (num_m * (H / c) * 2 >= ctx->sm_count) {
+        if (row_tiles * (H / c) * 2 >= slots) {
             bn = c;
             break;
         }
@@ -612,7 +734,8 @@ extern "C" int fu_oproj_forward(fu_oproj_ctx* ctx, const void* attn, const void*
     if (do_gemm) {
         rc = encode_2d(&p.tm_g, t.gather[t.sp_rank], L, K, oproj::BM, "gather");
         if (rc == FU_OK) rc = encode_2d(&p.tm_self, attn, S * L, cpm, oproj::BM, "attn");
-        if (rc == FU_OK) rc = encode_2d(&p.tm_w, w_o, H, K, static_cast<uint32_t>(bn), "w_o");
+        if (rc == FU_OK)
+            rc = encode_2d(&p.tm_w, w_o, H, K, static_cast<uint32_t>(pair ? bn / 2 : bn), "w_o");
         if (rc == FU_OK) rc = encode_2d(&p.tm_out, out, L, H, 32, "out");
         if (rc != FU_OK) return rc;
     }
@@ -631,10 +754,12 @@ extern "C" int fu_oproj_forward(fu_oproj_ctx* ctx, const void* attn, const void*
     p.sp_rank = t.sp_rank;
     p.num_m = static_cast<int32_t>(num_m);
     p.bn = bn;
-    p.stage_bytes = oproj::A_STAGE_BYTES + bn * oproj::BK * 2;
+    // Per CTA: 128 rows of X and bn (single) or bn / 2 (pair) rows of W_o.
+    p.stage_bytes = oproj::A_STAGE_BYTES + (pair ? bn / 2 : bn) * oproj::BK * 2;
     p.stages = oproj::RING_BYTES / p.stage_bytes;
+    if (p.stages > oproj::MAX_STAGES) p.stages = oproj::MAX_STAGES;
     p.num_n = static_cast<int32_t>(H / bn);
-    p.num_tiles = do_gemm ? p.num_m * p.num_n : 0;
+    p.num_tiles = do_gemm ? static_cast<int32_t>(row_tiles) * p.num_n : 0;
     p.k_blocks = static_cast<int32_t>(K / oproj::BK);
     // Push units of ~32 KiB: 8 to 128 rows (a power of two) of cpm columns.
     int slice_rows = 8;
@@ -645,17 +770,40 @@ extern "C" int fu_oproj_forward(fu_oproj_ctx* ctx, const void* attn, const void*
     p.wait_peers = (flags & FU_FWD_NO_PEER_WAIT) == 0 ? 1u : 0u;
     p.do_gather = do_gather ? 1u : 0u;
     p.do_gemm = do_gemm ? 1u : 0u;
-    const int64_t work = p.num_tiles > p.units ? p.num_tiles : p.units;
-    // At least one CTA, which advances the epoch (a push-only call of a world
-    // of one has nothing else to do).
-    const int grid = static_cast<int>(work < 1 ? 1 : work < ctx->sm_count ? work : ctx->sm_count);
+    int grid;
+    if (pair) {
+        // One pair per tile up to the co-resident pairs (push units ride along).
+        grid = 2 * static_cast<int>(p.num_tiles < ctx->max_pairs ? p.num_tiles : ctx->max_pairs);
+    } else {
+        const int64_t work = p.num_tiles > p.units ? p.num_tiles : p.units;
+        // At least one CTA, which advances the epoch (a push-only call of a
+        // world of one has nothing else to do).
+        grid = static_cast<int>(work < 1 ? 1 : work < ctx->sm_count ? work : ctx->sm_count);
+    }
     ctx->last_grid = grid;
     int prev = 0;
     cudaGetDevice(&prev);
     if (prev != t.device) cudaSetDevice(t.device);
-    oproj::oproj_exchange_kernel<<<grid, oproj::NUM_THREADS, oproj::SMEM_ALLOC,
-                                   static_cast<cudaStream_t>(stream)>>>(p);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e;
+    if (pair) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid, 1, 1);
+        cfg.blockDim = dim3(oproj::NUM_THREADS, 1, 1);
+        cfg.dynamicSmemBytes = oproj::SMEM_ALLOC;
+        cfg.stream = static_cast<cudaStream_t>(stream);
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = 2;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, oproj::oproj_exchange_kernel<true>, p);
+    } else {
+        oproj::oproj_exchange_kernel<false><<<grid, oproj::NUM_THREADS, oproj::SMEM_ALLOC,
+                                              static_cast<cudaStream_t>(stream)>>>(p);
+        e = cudaGetLastError();
+    }
     if (prev != t.device) cudaSetDevice(prev);
     if (e != cudaSuccess) return set_error(FU_ERR_CUDA, "launch failed: %s", cudaGetErrorString(e));
     ++ctx->calls;

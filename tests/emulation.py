@@ -136,7 +136,8 @@ class EmulatedOprojGroup:
             t.timeout_ns = int(timeout_s * 1e9)
             self.ops.append(_C.OprojOp(t))
 
-    def run(self, attn_outs, weights, outs, tokens):
+    def run(self, attn_outs, weights, outs, tokens, variant=0):
+        """``variant``: 0 automatic, or FU_FWD_SINGLE / FU_FWD_PAIR for the GEMM."""
         stream = _C.current_stream_handle(self.device.index or 0)
         base = _C.FU_FWD_NO_PEER_WAIT
         for r in range(self.S):
@@ -144,7 +145,8 @@ class EmulatedOprojGroup:
                                 base | _C.FU_OPROJ_GATHER_ONLY, stream)
         for r in range(self.S):
             self.ops[r].forward(attn_outs[r].data_ptr(), weights[r].data_ptr(), tokens,
-                                outs[r].data_ptr(), base | _C.FU_OPROJ_GEMM_ONLY, stream)
+                                outs[r].data_ptr(), base | _C.FU_OPROJ_GEMM_ONLY | variant,
+                                stream)
 
     def counters_reset(self):
         """Completion, work and ready counters are back at zero after a call."""

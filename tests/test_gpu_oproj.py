@@ -34,7 +34,7 @@ def world_inputs(S, H, q_heads, tokens, seed=0, exact=False):
     return attn, w
 
 
-def run_emulated(S, H, q_heads, tokens, attn, w, calls=1):
+def run_emulated(S, H, q_heads, tokens, attn, w, calls=1, variant=0):
     dev = torch.device("cuda", 0)
     group = EmulatedOprojGroup(sp_size=S, hidden_size=H, q_heads=q_heads,
                                max_local_tokens=tokens + 5)
@@ -44,7 +44,7 @@ def run_emulated(S, H, q_heads, tokens, attn, w, calls=1):
         outs = [torch.full((tokens, H), float("nan"), dtype=torch.bfloat16, device=dev)
                 for _ in range(S)]
         for _ in range(calls):
-            group.run(gattn, gw, outs, tokens)
+            group.run(gattn, gw, outs, tokens, variant=variant)
         torch.cuda.synchronize()
         assert group.status.value == 0, _C.decode_status(group.status.value)
         assert group.counters_reset()
@@ -77,8 +77,26 @@ def test_oproj_emulated_groups(S, H, q_heads, tokens):
         assert bad == 0, f"rank {r}: {bad} violations, max abs err {err}"
 
 
+@pytest.mark.parametrize("S,H,q_heads,tokens,variant", [
+    (2, 1024, 8, 300, "single"), (2, 1024, 8, 300, "pair"), (1, 4096, 32, 2000, "single"),
+    (1, 4096, 32, 2000, "pair"), (4, 2048, 16, 129, "pair"), (1, 512, 4, 1, "pair"),
+])
+def test_oproj_variants(S, H, q_heads, tokens, variant):
+    """The single-CTA and the CTA-pair GEMM (odd m-block counts leave the last
+    pair's second CTA without rows), tile widths 64 to 256."""
+    flag = {"single": _C.FU_FWD_SINGLE, "pair": _C.FU_FWD_PAIR}[variant]
+    attn, w = world_inputs(S, H, q_heads, tokens, seed=11)
+    topo = oracle.Topology(S, S, q_heads, q_heads, H)
+    got, _ = run_emulated(S, H, q_heads, tokens, attn, w, variant=flag)
+    want = oracle.o_proj_world(topo, attn, [w] * S, tokens)
+    for r in range(S):
+        bad, err = isclose_stats(got[r], want[r])
+        assert bad == 0, f"rank {r}: {bad} violations, max abs err {err}"
+
+
 @pytest.mark.parametrize("S,H,q_heads,tokens", [
     (1, 1024, 8, 65), (2, 512, 4, 300), (4, 1024, 8, 130), (8, 2048, 16, 17),
+    (1, 1024, 8, 600),
 ])
 def test_oproj_bit_exact_on_exact_inputs(S, H, q_heads, tokens):
     """Integer-valued operands: every order of the FP32 sums is exact, so the
