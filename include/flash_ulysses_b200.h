@@ -270,7 +270,8 @@ FU_API int64_t fu_oproj_sync_words(int64_t max_local_tokens);
 FU_API int fu_oproj_create(const fu_oproj_topology* topo, fu_oproj_ctx** out);
 FU_API int fu_oproj_destroy(fu_oproj_ctx* ctx);
 
-/* One call, one launch on `stream`:
+/* One call, one launch on `stream` (flags: FU_FWD_NO_PEER_WAIT, FU_FWD_SINGLE /
+ * FU_FWD_PAIR to force the GEMM variant, FU_OPROJ_GATHER_ONLY / FU_OPROJ_GEMM_ONLY):
  *   attn   BF16 [S * local_tokens, q_heads/S * 128], this rank's attention output
  *   w_o    BF16 [H, q_heads * 128]
  *   out    BF16 [local_tokens, H]
