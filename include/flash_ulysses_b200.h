@@ -155,7 +155,10 @@ typedef struct fu_qkv_topology {
 
 /* Create the per-rank operator state (tensor-map caches, epoch counter).
  * Replaces the descriptor set-up of the reference launcher
- * (flash_ulysses_kernel_hopper.cu:305-347). */
+ * (flash_ulysses_kernel_hopper.cu:305-347).  A context is not thread-safe:
+ * calls on one context (either operator) must not run concurrently on the
+ * host, since each call updates the context's caches and parameter block;
+ * different contexts are independent. */
 FU_API int fu_qkv_create(const fu_qkv_topology* topo, fu_qkv_ctx** out);
 FU_API int fu_qkv_destroy(fu_qkv_ctx* ctx);
 
