@@ -10,22 +10,26 @@
 // (torch.nn.Linear layout).  The reference stops at the forward exchange;
 // this operator is the step its outputs feed once attention has run.
 //
-// Per CTA, 192 threads in six warps:
+// Per CTA, 192 threads in six warps (single CTAs, or CTA pairs with tcgen05
+// cta_group::2 once L spans two 128-row m-blocks):
 //   warp 0     TMA producer: X tiles -- this rank's own heads straight from its
 //              attention output, the peers' heads from its gather buffer G
 //              once the m-block's ready counter is complete -- and W_o tiles
-//   warp 1     TMEM owner + tcgen05.mma issuer (M=128, N=bn, both K-major)
+//              (half of each tile's rows per CTA of a pair)
+//   warp 1     TMEM owner + tcgen05.mma issuer (M=128 or, on the pair's
+//              leader, M=256; N=bn; both operands K-major)
 //   warps 2-5  epilogue: TMEM -> BF16 -> swizzled staging -> TMA store of
 //              out.  Before it, warps 2-3 run the push side of the exchange:
-//              claims units (m-block, peer s, 8-row slice) from an atomic work
-//              counter, copies the slice's rows of this rank's attention output
-//              -- local reads -- into G_s with 16-byte posted stores (NVLink
-//              writes), fences, and bumps G_s's ready counter of that m-block.
+//              claim units (m-block, peer s, slice of ~32 KiB) from an atomic
+//              work counter, copy the slice's rows of this rank's attention
+//              output -- local reads -- into G_s with 16-byte posted stores
+//              (NVLink writes), fence, and bump G_s's ready counter of that
+//              m-block.
 // Units are taken in m-block order by whichever warps are running, so no CTA
 // depends on another being resident; every wait is bounded.
 //
 // Epochs: CTA 0 publishes "entered e" into every member's sync block; a
-// gather warp waits (bounded) until member s has entered e before its first
+// push warp waits (bounded) until member s has entered e before its first
 // store into G_s, so G_s is no longer read by s's previous call.  The ready
 // counters are reset by the last CTA of their owner once every tile has been
 // loaded; peers cannot count into the next call before the owner enters it.
@@ -47,7 +51,7 @@ constexpr int BM = 128;                         // token rows per tile = TMEM la
 constexpr int BN = 256;                         // widest tile: output columns (TMEM stride)
 constexpr int BK = 64;                          // one 128-byte swizzle row of K
 constexpr int UMMA_K = 16;
-constexpr int MAX_STAGES = 8;                   // 4 at bn = 256, 6 at 128, 8 at 64
+constexpr int MAX_STAGES = 8;                   // single CTA: 4 / 6 / 8 at bn = 256 / 128 / 64
 constexpr int NUM_THREADS = 192;
 constexpr int NUM_EPI_THREADS = 128;
 constexpr int UNIT_BYTES = 32 * 1024;           // target bytes of one push unit
@@ -56,7 +60,7 @@ constexpr int UNIT_BYTES = 32 * 1024;           // target bytes of one push unit
 // push (fenced per unit) runs below the GEMM's consumption rate; with all
 // four, every m-block completes late.
 constexpr int PUSH_WARPS = 2;
-constexpr int A_STAGE_BYTES = BM * BK * 2;      // 16 KiB, then bn * 128 bytes of W_o
+constexpr int A_STAGE_BYTES = BM * BK * 2;      // 16 KiB, then this CTA's rows of W_o
 constexpr int RING_BYTES = 4 * (A_STAGE_BYTES + BN * BK * 2);   // 192 KiB
 constexpr int OFF_RING = 0;
 constexpr int OFF_STG = OFF_RING + RING_BYTES;
