@@ -16,6 +16,10 @@ keywords, properties, ``ulysses_qkv_forward`` signature, output aliasing and
 * a device-side wait that gives up (``timeout_s``) or a position outside the
   RoPE cache sets a status word; the next call (or ``check()``) raises
   ``RuntimeError`` instead of hanging.
+
+Added (no counterpart in the reference): with ``output_projection=True``,
+``ulysses_o_proj_forward`` runs the inverse exchange after attention fused with
+the attention output projection.
 """
 
 from __future__ import annotations
