@@ -28,6 +28,11 @@ So this harness checks (a) at most ``--max-epilogue-violation-fraction``
 (1e-7) of the elements against the reference's epilogue and exchange applied
 to this build's own projection and (b) at most ``--max-violation-fraction``
 (1e-5) against the full reference path.
+
+``--o-proj`` (no counterpart in the reference) also runs the output side on
+each case's Q as the attention output: zero violations against an NCCL
+all_to_all of the source blocks followed by the FP32-accumulated projection,
+and the same per-call timing against NCCL all_to_all + cuBLAS.
 """
 
 import argparse
@@ -55,6 +60,9 @@ def parse_args():
     p.add_argument("--rtol", type=float, default=0.01)
     p.add_argument("--max-violation-fraction", type=float, default=1e-5)
     p.add_argument("--max-epilogue-violation-fraction", type=float, default=1e-7)
+    p.add_argument("--o-proj", action="store_true",
+                   help="also check and time the output side (inverse exchange fused with "
+                        "o_proj; no counterpart in the reference) on each case's Q")
     args = p.parse_args()
     if min(args.local_tokens) < 1 or args.warmup < 0 or args.iters < 1:
         p.error("local-tokens/iters must be positive; warmup must be nonnegative")
@@ -84,7 +92,8 @@ def main(args):
     ctx = FlashUlyssesContext(rank=rank, world_size=world,
                               max_local_tokens=max(args.local_tokens) + 128,
                               hidden_size=args.hidden_size, num_heads=args.q_heads,
-                              num_kv_heads=args.kv_heads, sp_size=S, control_group=gloo)
+                              num_kv_heads=args.kv_heads, sp_size=S, control_group=gloo,
+                              output_projection=args.o_proj)
     topo = oracle.Topology(world, S, args.q_heads, args.kv_heads, args.hidden_size)
     sp_group = None
     for start in range(0, world, S):
@@ -179,6 +188,38 @@ def main(args):
         dist.all_reduce(untouched, op=dist.ReduceOp.MIN)
         ok &= bool(untouched.item())
         say(f"  correctness: {'PASS' if ok else 'FAIL'} (all Q/K/V rows and output boundary)")
+        o_row = None
+        if args.o_proj:
+            # Q as the attention output; the reference side is an NCCL
+            # all_to_all of its source blocks, then the FP32-accumulated GEMM.
+            k_o = ctx.local_q_heads * 128
+            g_o = torch.Generator(device="cuda").manual_seed(4321 + rank // S)
+            w_o = (torch.randn(H, k_o, device="cuda", generator=g_o) * k_o ** -0.5).bfloat16()
+            attn = got[0]
+            y = ctx.ulysses_o_proj_forward(attn, w_o)
+            ctx.check()
+
+            def o_reference(fp32=True):
+                send = attn.reshape(S, L, -1).contiguous()
+                recv = torch.empty_like(send)
+                dist.all_to_all_single(recv, send, group=sp_group)
+                gathered = torch.cat(list(recv), dim=-1)
+                return oracle.o_proj(gathered, w_o) if fp32 else gathered @ w_o.t()
+
+            want_y = o_reference()
+            bad = (~torch.isclose(y.float(), want_y.float(), atol=args.atol,
+                                  rtol=args.rtol)).sum()
+            dist.all_reduce(bad)
+            o_ok = int(bad) == 0
+            ok &= o_ok
+            say(f"  o_proj: violations {int(bad)}/{y.numel() * world} "
+                f"{'ok' if o_ok else 'FAIL'}")
+            if not args.check_only:
+                ours_o = timed(lambda: ctx.ulysses_o_proj_forward(attn, w_o, out=y))
+                ref_o = timed(lambda: o_reference(fp32=False))
+                say(f"  o_proj ours: {ours_o:.3f} ms | NCCL all_to_all + cuBLAS: {ref_o:.3f} ms"
+                    f" | {ref_o / ours_o:.2f}x")
+                o_row = (ours_o, ref_o)
         if args.check_only:
             continue
         flops = 2 * L * H * ctx.packed_width
@@ -188,12 +229,17 @@ def main(args):
         say(f"  PyTorch: {ref:.3f} ms | GEMM-equivalent {flops / (ref * 1e9):.2f} TFLOP/s")
         say(f"  ours vs PyTorch: {ref / ours:.2f}x")
         if i > 0:
-            rows.append((L, ours, ref))
+            rows.append((L, ours, ref, o_row))
     if rows:
         say("\n| Local tokens (L) | ours (ms) | PyTorch+NCCL (ms) | vs PyTorch |")
         say("| ---: | ---: | ---: | ---: |")
-        for L, o, r in rows:
+        for L, o, r, _ in rows:
             say(f"| {L} | {o:.3f} | {r:.3f} | {r / o:.2f}x |")
+        if args.o_proj:
+            say("\n| Local tokens (L) | o_proj ours (ms) | NCCL all_to_all + cuBLAS (ms) | ratio |")
+            say("| ---: | ---: | ---: | ---: |")
+            for L, _, _, (o, r) in rows:
+                say(f"| {L} | {o:.3f} | {r:.3f} | {r / o:.2f}x |")
     ctx.close()
     dist.destroy_process_group(gloo)
     dist.destroy_process_group()
