@@ -135,3 +135,15 @@ int main(void) {{
     out = subprocess.run([str(exe)], capture_output=True, text=True)
     assert out.returncode == 0, (out.returncode, out.stderr)
     assert out.stdout.startswith("ok ")
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="no host C compiler")
+def test_integration_c_example_compiles(tmp_path):
+    """The C example in INTEGRATION.md compiles against the header as written."""
+    text = (HEADER.parent.parent / "INTEGRATION.md").read_text()
+    blocks = re.findall(r"```c\n(.*?)```", text, re.S)
+    assert blocks, "no C example found"
+    src = tmp_path / "example.c"
+    src.write_text(blocks[0].replace('#include "flash_ulysses_b200.h"', f'#include "{HEADER}"'))
+    subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", "-c", str(src),
+                    "-o", str(tmp_path / "example.o")], check=True)
