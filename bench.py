@@ -9,7 +9,13 @@ latency (max over ranks) and the GEMM-equivalent TFLOP/s per GPU.
 
 Launch: ``python bench.py [--gpus N --steps K --warmup W]``; for N > 1 under
 ``torch.distributed.run`` (one process per GPU).  ``--impl reference`` times
-the reference's PyTorch path on the host CPU (the oracle port) instead.
+the reference's PyTorch path on the host CPU instead (the oracle port of
+tests/torch_base.py:48-76, run as N gloo processes with the real all-to-all;
+rank 0 alone runs it and the other ranks exit at once).
+
+Every rank makes the same sequence of calls and collectives, on error paths
+too: each call is a collective of the SP group, so a rank that made one call
+more than its peers would wait for them until its bounded wait gives up.
 """
 
 from __future__ import annotations
@@ -75,18 +81,11 @@ def measured_peaks():
 
 NVLINK_GBS = 770.0      # measured peer copy per direction on this pool (900 nominal)
 
-
-def profiled_traffic():
-    """DRAM bytes per launch of the fused kernel from the committed ncu summary."""
-    path = ROOT / "profiles" / "fused_qkv_exchange_c1shape.md"
-    if not path.exists():
-        return None, None
-    info = {}
-    for line in path.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch_L"):
-            key, val = line.split(":", 1)
-            info[int(key.rsplit("L", 1)[1])] = float(val.strip())
-    return info, path.name
+# DRAM bytes (read + write) per launch of the fused kernel at the c1 shape,
+# world of one, from ncu captures (dram__bytes_read.sum + dram__bytes_write.sum;
+# profiles/fused_qkv_exchange_c1shape.md).  Keyed by tokens per rank.
+PROFILED_TRAFFIC = {4096: 186390016.0}
+PROFILED_TRAFFIC_SOURCE = "ncu capture, profiles/fused_qkv_exchange_c1shape.md"
 
 
 # ---------------------------------------------------------------- clocks
@@ -144,32 +143,61 @@ class ClockSampler:
 
 
 class NvlinkCounter:
-    """Cumulative NVLink data bytes sent/received by this GPU (NVML field
-    values, read-only), or None where the driver does not expose them."""
+    """Cumulative NVLink bytes sent/received by this GPU from NVML field
+    values (read-only).  Drivers differ in which fields and scopes they
+    support, so several are tried in order; ``source`` names the one in use,
+    ``errors`` the NVML return codes of those that failed."""
 
-    def __init__(self, device_index):
+    ALL_LINKS = 0xFFFFFFFF
+
+    def __init__(self, device_index, links=18):
         self.ok = False
+        self.source = None
+        self.errors = {}
         try:
             import pynvml
 
             pynvml.nvmlInit()
             self.nvml = pynvml
             self.handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
-            self.ok = self.read() is not None
-        except Exception:
-            self.ok = False
+        except Exception as e:          # no NVML: report why
+            self.errors["nvml"] = f"{type(e).__name__}: {e}"[:120]
+            return
+        n = pynvml
+        tx_rx = [("throughput_data", n.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_TX,
+                  n.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_RX, 1024),       # KiB counters
+                 ("count_bytes", n.NVML_FI_DEV_NVLINK_COUNT_XMIT_BYTES,
+                  n.NVML_FI_DEV_NVLINK_COUNT_RCV_BYTES, 1)]
+        self.variants = []
+        for name, tx, rx, unit in tx_rx:
+            self.variants.append((f"{name} all-links scope", [(tx, self.ALL_LINKS)],
+                                  [(rx, self.ALL_LINKS)], unit))
+            self.variants.append((f"{name} summed over links 0..{links - 1}",
+                                  [(tx, l) for l in range(links)],
+                                  [(rx, l) for l in range(links)], unit))
+        for v in self.variants:
+            if self._read(v) is not None:
+                self.variant, self.source, self.ok = v, v[0], True
+                break
+
+    def _read(self, variant):
+        name, tx, rx, unit = variant
+        try:
+            vals = self.nvml.nvmlDeviceGetFieldValues(self.handle, tx + rx)
+        except Exception as e:
+            self.errors[name] = f"{type(e).__name__}: {e}"[:120]
+            return None
+        codes = sorted({v.nvmlReturn for v in vals})
+        if codes != [0]:
+            self.errors[name] = f"nvmlReturn {codes}"
+            return None
+        total = [0, 0]
+        for i, v in enumerate(vals):
+            total[0 if i < len(tx) else 1] += v.value.ullVal * unit
+        return total
 
     def read(self):
-        n = self.nvml
-        try:
-            vals = n.nvmlDeviceGetFieldValues(
-                self.handle, [n.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_TX,
-                              n.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_RX])
-            if any(v.nvmlReturn != 0 for v in vals):
-                return None
-            return [v.value.ullVal * 1024 for v in vals]      # KiB counters
-        except Exception:
-            return None
+        return self._read(self.variant) if self.ok else None
 
 
 # ---------------------------------------------------------------- helpers
@@ -185,6 +213,37 @@ def rendezvous(world, group=None):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier(group=group)
+
+
+FAILED = []            # host-side errors of guarded steps (see ``guarded``)
+
+
+def healthy(ctx, world, group, what):
+    """Synchronise, then agree over the control group whether any rank's
+    context reported a device-side error (or a call raised on the host);
+    every rank raises together, so no rank is left waiting in a collective
+    for one that gave up."""
+    torch.cuda.synchronize()
+    bad = torch.tensor([1 if ctx._status.value or FAILED else 0], dtype=torch.int32)
+    if world > 1:
+        dist.all_reduce(bad, op=dist.ReduceOp.MAX, group=group)
+    if int(bad.item()):
+        raise RuntimeError(f"{what}: a rank reported an error (this rank: status "
+                           f"0x{ctx._status.value:x}, host {FAILED[:1]})")
+
+
+def guarded(fn, failed):
+    """A step that stops issuing calls after its first host-side error but
+    keeps every collective of the timing loop (the error is raised by
+    ``healthy`` afterwards, on every rank at once)."""
+    def step(i):
+        if failed:
+            return
+        try:
+            fn(i)
+        except RuntimeError as e:
+            failed.append(str(e))
+    return step
 
 
 def make_inputs(world, rank, tokens, seed):
@@ -254,42 +313,83 @@ def torch_reference_step(x, pos, params, sp, group):
 
 
 # ---------------------------------------------------------------- CPU leg
-def cpu_oracle_time(tokens, sp, budget_s=20.0, steps=None, warmup=1):
-    """One rank's reference PyTorch path on the host cores (the oracle port):
-    projection + norm + RoPE + pack, and the receive-side copy of the
-    exchange.  Returns (ms per step at the full workload, sample description,
-    threads)."""
+def _free_port():
+    import socket
+
+    with socket.socket() as sock:
+        sock.bind(("127.0.0.1", 0))
+        return sock.getsockname()[1]
+
+
+def _cpu_rank_worker(rank, sp, port, shape, tokens, steps, warmup, budget_s, threads, out):
+    """One rank of the reference's PyTorch path on host cores (the oracle port
+    of tests/torch_base.py:48-76: projection, norm, RoPE, pack, gloo
+    all_to_all_single, unpack).  Runs in a spawned process; rank 0 puts
+    (per-step seconds at the sample size, sample tokens) on ``out``."""
+    import datetime
+
+    torch.set_num_threads(threads)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=sp, timeout=datetime.timedelta(seconds=600))
     from flash_ulysses_b200.workloads import make_parameters, make_rank_inputs
     from oracle import ulysses_oracle as oracle
 
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    packed = (Q_HEADS + 2 * KV_HEADS) * 128
-    topo = oracle.Topology(sp, sp, Q_HEADS, KV_HEADS, HIDDEN)
-    params = make_parameters(HIDDEN, packed, MAX_POS, seed=0)
+    hidden, q_heads, kv_heads, max_pos = SHAPES[shape]
+    topo = oracle.Topology(sp, sp, q_heads, kv_heads, hidden)
+    params = make_parameters(hidden, topo.packed_width, max_pos, seed=0)
 
-    def one(n):
-        x, pos = make_rank_inputs(HIDDEN, n, MAX_POS, rank=0, sp_size=sp, seed=0)
+    def timed(x, pos):
+        dist.barrier()
         t0 = time.perf_counter()
-        send = oracle.rank_send(topo, x, pos, params)
-        received = torch.empty_like(send)
-        received.copy_(send)                      # stands in for the all-to-all
-        oracle.unpack(topo, received, n)
-        return time.perf_counter() - t0
+        oracle.rank_forward_gloo(topo, x, pos, params, None)
+        t = torch.tensor([time.perf_counter() - t0], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)           # max over ranks
+        return float(t.item())
 
+    # Bounded sample: halve the tokens per rank until the whole run fits the budget.
     sample = tokens
-    first = one(sample)
-    while first > budget_s / 4 and sample > 128:
+    while True:
+        x, pos = make_rank_inputs(hidden, sample, max_pos, rank=rank, sp_size=sp, seed=0)
+        first = timed(x, pos)
+        if first * (steps + warmup) <= budget_s or sample <= 128:
+            break
         sample //= 2
-        first = one(sample)
-    n_steps = steps if steps is not None else max(1, min(5, int(budget_s / max(first, 1e-3))))
-    for _ in range(warmup):
-        one(sample)
-    times = [one(sample) for _ in range(n_steps)]
+    for _ in range(max(warmup - 1, 0)):
+        timed(x, pos)
+    times = [timed(x, pos) for _ in range(steps)]
+    if rank == 0:
+        out.put((times, sample))
+    dist.destroy_process_group()
+
+
+def cpu_reference_time(tokens, sp, steps, warmup, budget_s, shape):
+    """The reference's PyTorch path as ``sp`` gloo processes on this host's
+    cores with the real all-to-all.  Returns (ms per step at the full
+    workload, sample description, threads in total)."""
+    import multiprocessing as mp
+
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    threads = max(1, (cores or 1) // sp)
+    ctx = mp.get_context("spawn")          # never fork a process that may hold a CUDA context
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_cpu_rank_worker,
+                         args=(r, sp, port, shape, tokens, steps, warmup, budget_s, threads, out))
+             for r in range(sp)]
+    for proc in procs:
+        proc.start()
+    try:
+        times, sample = out.get(timeout=budget_s * 3 + 600)
+    finally:
+        for proc in procs:
+            proc.join(timeout=120)
+            if proc.is_alive():
+                proc.kill()
     per = statistics.mean(times) * tokens / sample * 1e3
-    desc = (f"{n_steps} steps of {sample} of {tokens} tokens/rank, one rank's compute + "
-            f"receive copy, scaled x{tokens / sample:g}")
-    return per, desc, threads
+    desc = (f"{sp} gloo process(es) x {threads} threads (the reference PyTorch path with "
+            f"all_to_all_single), {len(times)} steps of {sample} of {tokens} tokens/rank, "
+            f"max over ranks, scaled x{tokens / sample:g}")
+    return per, desc, threads * sp
 
 
 def reference_arm(args):
@@ -297,8 +397,8 @@ def reference_arm(args):
     if rank != 0:
         return
     tokens, sp = args.tokens, max(args.gpus, world)
-    per, desc, threads = cpu_oracle_time(tokens, sp, budget_s=120.0 / max(args.steps, 1),
-                                         steps=args.steps, warmup=args.warmup)
+    per, desc, cores = cpu_reference_time(tokens, sp, args.steps, args.warmup, 120.0,
+                                          args.shape)
     flops = 2 * tokens * HIDDEN * (Q_HEADS + 2 * KV_HEADS) * 128
     line = {
         "metric": METRIC, "value": round(per, 4), "unit": "ms", "impl": "reference",
@@ -307,7 +407,7 @@ def reference_arm(args):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": workload_config(args.gpus, tokens),
         "tflops_per_gpu": round(flops / (per * 1e-3) / 1e12, 3),
-        "cpu_baseline": {"value": round(per, 4), "unit": "ms", "cores": threads,
+        "cpu_baseline": {"value": round(per, 4), "unit": "ms", "cores": cores,
                          "kind": "port", "sample": desc},
         "e2e": {"value": round(per, 4), "unit": "ms", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -337,9 +437,11 @@ def main():
     torch.cuda.set_device(local)
     group = None
     if world > 1:
+        import datetime
+
         dist.init_process_group("nccl", device_id=torch.device("cuda", local),
-                                timeout=__import__("datetime").timedelta(seconds=120))
-        group = dist.new_group(backend="gloo")
+                                timeout=datetime.timedelta(seconds=120))
+        group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=180))
     from flash_ulysses_b200 import FlashUlyssesContext
 
     tokens = args.tokens
@@ -349,25 +451,31 @@ def main():
                               sp_size=n, control_group=group, output_projection=True)
     sets = [make_inputs(n, rank, tokens, seed=s) for s in range(ROTATE)]
 
-    def step(i):
+    failed = FAILED
+
+    def call(i):
         x, pos, p = sets[i % ROTATE]
         return ctx.ulysses_qkv_forward(x, p["qkv_weight"], pos, p["q_norm_weight"],
                                        p["k_norm_weight"], p["rope_cache"],
                                        q_epsilon=p["q_epsilon"], k_epsilon=p["k_epsilon"])
 
+    step = guarded(call, failed)
     for i in range(args.warmup):
         step(i)
-    torch.cuda.synchronize()
+    healthy(ctx, n, group, "warm-up")
     # Soak ~0.5 s so the clock record reflects steady load, then time K steps.
+    # The number of soak calls is fixed before the soak and equal on every
+    # rank (from the max-over-ranks latency of a few timed calls): a loop
+    # bounded by each rank's own clock could end after different call counts.
+    est_ms = time_steps(step, 5, n, group)
+    healthy(ctx, n, group, "calibration")
+    soak_calls = int(min(5000, max(50, 500.0 / max(est_ms, 1e-3))))
     sampler = ClockSampler(torch.cuda.current_device())
     sampler.start()
-    t0 = time.perf_counter()
-    i = 0
-    while time.perf_counter() - t0 < 0.5:
-        step(i)
-        i += 1
-        if i % 50 == 0:
-            torch.cuda.synchronize()
+    for c0 in range(0, soak_calls, 50):
+        for i in range(c0, min(c0 + 50, soak_calls)):
+            step(i)
+        healthy(ctx, n, group, "soak")
     epoch0 = ctx.epoch
     nvl = NvlinkCounter(torch.cuda.current_device()) if n > 1 else None
     nvl0 = nvl.read() if nvl is not None and nvl.ok else None
@@ -375,7 +483,7 @@ def main():
     nvl1 = nvl.read() if nvl0 is not None else None
     clocks = sampler.stop()
     launches = ctx.epoch - epoch0
-    ctx.check()
+    healthy(ctx, n, group, "timed steps")
 
     flops = 2 * tokens * HIDDEN * ctx.packed_width
     tflops = flops / (ms * 1e-3) / 1e12
@@ -391,14 +499,22 @@ def main():
     if n > 1:
         nvlink = {"algorithmic_bytes_per_call": int(nvl_bytes),
                   "algorithmic_gbs": round(nvl_bytes / (ms * 1e-3) / 1e9, 1),
-                  "link_gbs_per_direction": NVLINK_GBS}
+                  "link_gbs_per_direction": NVLINK_GBS,
+                  "frac_of_link": round(nvl_bytes / (ms * 1e-3) / 1e9 / NVLINK_GBS, 4)}
         if nvl0 is not None and nvl1 is not None:
             dt = ms * 1e-3 * args.steps
+            nvlink["measured_source"] = f"NVML {nvl.source}"
+            nvlink["measured_tx_bytes_per_call"] = int((nvl1[0] - nvl0[0]) / args.steps)
+            nvlink["measured_rx_bytes_per_call"] = int((nvl1[1] - nvl0[1]) / args.steps)
             nvlink["measured_tx_gbs"] = round((nvl1[0] - nvl0[0]) / dt / 1e9, 1)
             nvlink["measured_rx_gbs"] = round((nvl1[1] - nvl0[1]) / dt / 1e9, 1)
+        else:
+            nvlink["measured"] = ("unavailable: NVML NVLink byte counters not readable "
+                                  f"({nvl.errors if nvl is not None else 'no counter'})")[:400]
 
     # The reference harness's per-call method (rendezvous between calls).
     iso = time_isolated(step, min(args.steps, 20), n, group)
+    healthy(ctx, n, group, "isolated calls")
 
     # e2e: through the public API from pinned host memory, every step's inputs
     # uploaded and its Q/K/V read back inside the timed region.  Uploads run on
@@ -440,6 +556,8 @@ def main():
                 h.copy_(d, non_blocking=True)
         read_back.record(down)
 
+    e2e_call = guarded(e2e_step, failed)
+
     def time_e2e(steps):
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
@@ -447,16 +565,17 @@ def main():
         start.record()
         up.wait_stream(main_stream)
         for i in range(steps):
-            e2e_step(i)
+            e2e_call(i)
         main_stream.wait_event(read_back)         # the last read-back is inside the region
         end.record()
         rendezvous(n, group)
         return max_over_ranks(start.elapsed_time(end) / steps, n)
 
     for i in range(2):
-        e2e_step(i)
-    torch.cuda.synchronize()
+        e2e_call(i)
+    healthy(ctx, n, group, "e2e warm-up")
     e2e_ms = time_e2e(args.steps)
+    healthy(ctx, n, group, "e2e")
     h2d = dx[0].numel() * 2 + dp[0].numel() * 8
     d2h = sum(t.numel() * 2 for t in outs_h)
 
@@ -475,26 +594,27 @@ def main():
             s_sets = sets if L == tokens else [make_inputs(n, rank, L, seed=s)
                                                for s in range(ROTATE)]
 
-            def s_step(i, s_sets=s_sets):
+            def s_call(i, s_sets=s_sets):
                 x, pos, p = s_sets[i % ROTATE]
                 ctx.ulysses_qkv_forward(x, p["qkv_weight"], pos, p["q_norm_weight"],
                                         p["k_norm_weight"], p["rope_cache"],
                                         q_epsilon=p["q_epsilon"], k_epsilon=p["k_epsilon"])
 
+            s_step = guarded(s_call, failed)
             for i in range(3):
                 s_step(i)
             t = time_steps(s_step, 20, n, group)
+            healthy(ctx, n, group, f"sweep L={L}")
             f = 2 * L * HIDDEN * ctx.packed_width
             sweep[str(L)] = {"ms": round(t, 5), "tflops_per_gpu": round(f / (t * 1e-3) / 1e12, 1),
                              "grid": ctx._op.last_grid,
                              "weight_read_gbs": round(HIDDEN * ctx.packed_width * 2 / (t * 1e-3)
                                                       / 1e9, 1)}
             del s_sets
-        ctx.check()
 
     cpu = None
     if rank == 0 and n == 1 and not args.no_cpu_baseline:
-        per, desc, threads = cpu_oracle_time(tokens, n)
+        per, desc, threads = cpu_reference_time(tokens, 1, 5, 1, 20.0, args.shape)
         cpu = {"value": round(per, 3), "unit": "ms", "cores": threads, "kind": "port",
                "sample": desc}
 
@@ -514,9 +634,11 @@ def main():
                   for _ in range(ROTATE)]
         o_out = torch.empty(tokens, HIDDEN, dtype=torch.bfloat16, device="cuda")
 
-        def o_step(i):
+        def o_call(i):
             a, w = o_sets[i % ROTATE]
             ctx.ulysses_o_proj_forward(a, w, out=o_out)
+
+        o_step = guarded(o_call, failed)
 
         def o_torch_step(i):
             a, w = o_sets[i % ROTATE]
@@ -533,7 +655,7 @@ def main():
         o_ms = time_steps(o_step, args.steps, n, group)
         o_proj_launches[0] = ctx._oproj.calls - o_launches0
         o_torch_ms = time_steps(o_torch_step, min(args.steps, 20), n, group)
-        ctx.check()
+        healthy(ctx, n, group, "o_proj")
         o_flops = 2 * tokens * o_k * HIDDEN
         return {"ms": round(o_ms, 5),
                 "tflops_per_gpu": round(o_flops / (o_ms * 1e-3) / 1e12, 1),
@@ -548,8 +670,8 @@ def main():
     except Exception as e:  # reported in the JSON line instead of aborting it
         o_proj = {"error": f"{type(e).__name__}: {e}"[:300]}
 
-    traffic_map, traffic_src = profiled_traffic()
-    traffic = None if not traffic_map else traffic_map.get(tokens)
+    traffic = PROFILED_TRAFFIC.get(tokens) if HIDDEN == 4096 and Q_HEADS == 32 else None
+    traffic_src = PROFILED_TRAFFIC_SOURCE if traffic is not None else None
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(ms, 5), "unit": "ms", "n_gpus": n,

@@ -22,6 +22,7 @@ FU_SYNC_WORDS = 64
 FU_SYNC_ENTRY = 8
 FU_SYNC_COUNTER = 32
 FU_SYNC_EPOCH = 33
+FU_SYNC_FAILED = 35
 FU_FWD_NO_PEER_WAIT = 1
 
 

@@ -13,9 +13,13 @@ keywords, properties, ``ulysses_qkv_forward`` signature, output aliasing and
   broker-based ``TKParallelTensor``; the exit barrier is fused into the kernel
   and uses per-call epoch flags instead of a separate multicast barrier
   launch;
-* a device-side wait that gives up (``timeout_s``) or a position outside the
-  RoPE cache sets a status word; the next call (or ``check()``) raises
-  ``RuntimeError`` instead of hanging.
+* a device-side wait that gives up (``timeout_s``, default 30 s) or a
+  position outside the RoPE cache sets a status word; the next call (or
+  ``check()``) raises ``RuntimeError`` instead of hanging, and
+  ``ulysses_qkv_forward(..., check=True)`` raises for the failing call itself.
+  A call that starts on the device after an earlier call gave up a wait (one
+  queued behind a failed call) stores nothing into any receive buffer and
+  waits for no peer.
 
 Added (no counterpart in the reference): with ``output_projection=True``,
 ``ulysses_o_proj_forward`` runs the inverse exchange after attention fused with
@@ -52,7 +56,7 @@ class FlashUlyssesContext:
         head_dim=128,
         sp_size=2,
         control_group=None,
-        timeout_s=5.0,
+        timeout_s=30.0,
         output_projection=False,
     ):
         self.rank, self.world_size = rank, world_size
@@ -192,6 +196,7 @@ class FlashUlyssesContext:
         *,
         q_epsilon=1e-6,
         k_epsilon=1e-6,
+        check=False,
         _projection_out=None,
     ):
         """Return BF16 (q, k, v), each with L * sp_size rows.
@@ -201,6 +206,12 @@ class FlashUlyssesContext:
         positions int64 [L], norm weights FP32 [128], and a NeoX RoPE cache
         FP32 [max_position, 128] containing [cos(64), sin(64)]. Positions must
         index the cache. Epsilons must be positive. The caller crops padding.
+
+        ``check=True`` waits for this call to finish on the current stream
+        and raises ``RuntimeError`` if it reported a device-side error (a peer
+        that never joined it, a position outside the cache), so the caller
+        learns that these outputs are invalid; by default errors surface on
+        the next call or ``check()``, without a synchronisation per call.
 
         ``_projection_out`` is test instrumentation: a BF16 [L, packed_width]
         tensor that also receives this rank's BF16 projection ``x @ W``.
@@ -214,6 +225,11 @@ class FlashUlyssesContext:
         _C.launch(hidden_states, qkv_weight, positions, q_norm_weight, k_norm_weight,
                   rope_cache, self._op, q_epsilon=q_epsilon, k_epsilon=k_epsilon,
                   gemm_out=_projection_out)
+        if check:
+            torch.cuda.current_stream(self.device).synchronize()
+            if self._status.value:
+                raise RuntimeError("this call failed on the device: "
+                                   + _C.decode_status(self._status.value))
         views = self._views.get(local_tokens)
         if views is None:
             output_tokens = local_tokens * self.sp_size
@@ -275,12 +291,14 @@ class FlashUlyssesContext:
             raise RuntimeError("device-side error: " + _C.decode_status(self._status.value))
 
     def clear_error(self):
-        """Reset the status word and the completion counter after a reported error
-        (call only when no launch of this context is in flight)."""
+        """Reset the status word, the completion counters and the operators'
+        failed marks after a reported error (call only when no launch of this
+        context is in flight)."""
         torch.cuda.synchronize(self.device)
-        self.barrier.data_[_C.FU_SYNC_COUNTER].zero_()
-        if self.o_barrier is not None:
-            self.o_barrier.data_[_C.FU_SYNC_COUNTER].zero_()
+        for block in (self.barrier, self.o_barrier):
+            if block is not None:
+                block.data_[_C.FU_SYNC_COUNTER].zero_()
+                block.data_[_C.FU_SYNC_FAILED].zero_()
         torch.cuda.synchronize(self.device)
         self._status.clear()
 

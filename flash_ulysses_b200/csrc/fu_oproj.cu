@@ -157,6 +157,19 @@ __device__ void run_gather(const OprojParams& p, uint32_t epoch, volatile int* a
     const uint32_t magic = 0xFFFFFFFFu / static_cast<uint32_t>(cpr) + 1u;
     const int dst_row = p.K / 8;                  // 16-byte chunks per row of G
     uint32_t entered = 0;                         // members known to have entered this epoch
+    // A call queued behind one that failed (this operator's sticky
+    // FU_SYNC_FAILED word, in local device memory) pushes nothing and waits
+    // for nothing; the abort flag stops this CTA's producer and MMA issuer too.
+    if (p.sp_size > 1) {
+        int bad = 0;
+        if (lane == 0)
+            bad = *reinterpret_cast<volatile const uint32_t*>(p.sync[p.sp_rank] +
+                                                            FU_SYNC_FAILED) != 0u;
+        if (__shfl_sync(0xffffffffu, bad, 0)) {
+            *abort_flag = 1;
+            return;
+        }
+    }
     while (true) {
         int u = 0;
         if (lane == 0) u = static_cast<int>(atomicAdd(work, 1u));
@@ -564,6 +577,8 @@ oproj_exchange_kernel(const __grid_constant__ OprojParams p) {
             volatile uint32_t* vs = my_sync;
             vs[FU_SYNC_COUNTER] = 0u;
             vs[FU_SYNC_EPOCH] = epoch;
+            if ((old >> 16) != 0 || aborted)
+                if (p.sp_size > 1) vs[FU_SYNC_FAILED] = 1u;   // later calls skip
             if (p.do_gather) vs[SYNC_WORK] = 0u;
             if (p.do_gemm)
                 for (int m = 0; m < p.num_m; ++m) vs[FU_OPROJ_READY + m] = 0u;
@@ -675,7 +690,7 @@ extern "C" int fu_oproj_create(const fu_oproj_topology* topo, fu_oproj_ctx** out
     auto* ctx = new fu_oproj_ctx();
     ctx->max_pairs = pairs;
     ctx->topo = *topo;
-    if (ctx->topo.timeout_ns == 0) ctx->topo.timeout_ns = 5000000000ull;
+    if (ctx->topo.timeout_ns == 0) ctx->topo.timeout_ns = FU_DEFAULT_TIMEOUT_NS;
     ctx->sm_count = sms;
     std::memset(&ctx->params, 0, sizeof(ctx->params));
     *out = ctx;

@@ -242,6 +242,16 @@ __device__ __forceinline__ void tmem_ld_16cols(uint32_t taddr, uint32_t (&r)[16]
         : "memory");
 }
 
+// 32 lanes x 8 consecutive FP32 columns.
+__device__ __forceinline__ void tmem_ld_8cols(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+          "=r"(r[6]), "=r"(r[7])
+        : "r"(taddr)
+        : "memory");
+}
+
 // Inverse of tmem_ld_32cols: thread i of the warp writes columns
 // [col, col+32) of TMEM lane (lane_base + i).
 __device__ __forceinline__ void tmem_st_32cols(uint32_t taddr, const uint32_t (&r)[32]) {
@@ -319,6 +329,7 @@ __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+
 
 __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu_u32(uint32_t* p, uint32_t v) {
     uint32_t old;
@@ -419,6 +430,16 @@ __device__ __forceinline__ uint32_t map_cluster_smem(uint32_t local_smem_addr, u
     uint32_t r;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
     return r;
+}
+
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t cluster_addr) {
+    uint32_t v;
+    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(cluster_addr) : "memory");
+    return v;
 }
 
 __device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t cluster_addr) {

@@ -132,6 +132,13 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
     return __bfloat1622float2(b);
 }
 
+// 1 / sqrt(mean + eps) for a sum of 128 squares, with the rounding points of
+// torch's CPU operators: the mean (an exact scaling), the FP32 addition of
+// eps, a correctly rounded square root and a correctly rounded reciprocal.
+__device__ __forceinline__ float norm_scale(float sum_sq, float eps) {
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(sum_sq * (1.0f / 128.0f), eps)));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&b);
@@ -310,23 +317,57 @@ struct Bars {
           tempty(base + 16 * MAX_STAGES + 16), mma_done(base + 16 * MAX_STAGES + 32) {}
 };
 
+// Whether an earlier call of this operator gave up a wait (the sticky
+// FU_SYNC_FAILED word of this rank's own sync block, in device memory: a read
+// of the host-mapped status word from every CTA would cost a serialised
+// host-memory round trip each).  Read early by the thread that runs the entry
+// barrier, so the read overlaps the main loop.
+__device__ __forceinline__ int32_t status_at_start(const QkvParams& p) {
+    if (threadIdx.x != 64 || p.sp_size == 1) return 0;
+    return static_cast<int32_t>(
+        *reinterpret_cast<volatile const uint32_t*>(p.sync[p.sp_rank] + FU_SYNC_FAILED));
+}
+
 // Entry barrier, run by the 4 epilogue warps before their CTA's first store
 // into a peer's buffer: one thread waits (bounded) until every SP member has
-// started this call's epoch, then the warps meet on named barrier 1.
-__device__ __forceinline__ void wait_peers_entered(const QkvParams& p, uint32_t epoch) {
-    if (p.sp_size > 1 && p.wait_peers && threadIdx.x == 64) {
-        const uint32_t* entry = p.sync[p.sp_rank] + FU_SYNC_ENTRY;
-        const uint64_t t0 = globaltimer_ns();
-        for (int s = 0; s < p.sp_size; ++s) {
-            while (static_cast<int32_t>(ld_acquire_sys_u32(entry + s) - epoch) < 0) {
-                if (globaltimer_ns() - t0 > p.timeout_ns) {
-                    report_status(p.status, FU_DEV_PEER_TIMEOUT, 16 + s);
-                    break;
+// started this call's epoch, then the warps meet on named barrier 1.  Returns
+// false -- and the CTA stores nothing -- when an earlier call of this operator
+// failed (this queued call must neither wait for peers nor write into them)
+// or when the wait gives up.  Either raises the
+// CTA's abort flag, so the producer and MMA issuer stop too.  In a CTA pair
+// the partner's abort flag is raised as well (over distributed shared
+// memory), since the pair's MMAs and accumulator hand-offs involve both.
+__device__ __forceinline__ bool wait_peers_entered(const QkvParams& p, uint32_t epoch,
+                                                   volatile int* abort_flag, bool pair,
+                                                   int32_t status_seen) {
+    if (threadIdx.x == 64) {
+        bool give_up = false;
+        if (*abort_flag) {
+            // Another role of this CTA (or of its cluster) already gave up.
+        } else if (status_seen != 0) {
+            give_up = true;
+        } else if (p.sp_size > 1 && p.wait_peers) {
+            const uint32_t* entry = p.sync[p.sp_rank] + FU_SYNC_ENTRY;
+            const uint64_t t0 = globaltimer_ns();
+            for (int s = 0; s < p.sp_size && !give_up; ++s) {
+                while (static_cast<int32_t>(ld_acquire_sys_u32(entry + s) - epoch) < 0) {
+                    if (globaltimer_ns() - t0 > p.timeout_ns) {
+                        report_status(p.status, FU_DEV_PEER_TIMEOUT, 16 + s);
+                        give_up = true;
+                        break;
+                    }
                 }
             }
         }
+        if (give_up) {
+            *abort_flag = 1;
+            if (pair)
+                st_cluster_u32(map_cluster_smem(smem_u32(const_cast<int*>(abort_flag)),
+                                                cluster_ctarank() ^ 1u), 1u);
+        }
     }
     named_bar_sync(1, NUM_EPI_THREADS);
+    return *abort_flag == 0;
 }
 
 // ------------------------------------------------------------ roles
@@ -354,8 +395,8 @@ __device__ void run_producer(const QkvParams& p, const Sched& sc, uint8_t* smem,
         const uint32_t stage_tx = kPair ? 2u * (A_STAGE_BYTES + chunks * B_CHUNK_BYTES)
                                         : R::STAGE_TX;
         for (int kb = it.kb0; kb < it.kb1; ++kb) {
-            if (!fu_wait_parity(b.empty + 8 * stage, phase ^ 1u, abort_flag, p.timeout_ns,
-                                p.status, W_EMPTY)) {
+            if (*abort_flag || !fu_wait_parity(b.empty + 8 * stage, phase ^ 1u, abort_flag,
+                                               p.timeout_ns, p.status, W_EMPTY)) {
                 ok = false;
                 break;
             }
@@ -421,8 +462,8 @@ __device__ void run_mma(const QkvParams& p, const Sched& sc, uint8_t* smem, uint
     for (; ok && next_item(p, sc, walk, it); ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!fu_wait_parity(b.tempty + 8 * acc, acc_phase ^ 1u, abort_flag, p.timeout_ns,
-                            p.status, W_TEMPTY)) {
+        if (*abort_flag || !fu_wait_parity(b.tempty + 8 * acc, acc_phase ^ 1u, abort_flag,
+                                           p.timeout_ns, p.status, W_TEMPTY)) {
             ok = false;
             break;
         }
@@ -541,22 +582,37 @@ __device__ __forceinline__ void emit_head(const QkvParams& p, uint32_t taddr, in
 
     float scale = 0.f;
     if (comp < 2) {
-        float ss = 0.f;
+        // Sum of the 128 squares in the order of torch's CPU reduction, so the
+        // result is bit-identical: four accumulators of eight lanes, where
+        // accumulator k, lane l sums columns 32c + 8k + l over c = 0..3; the
+        // accumulators are added in order k = 0..3 (into lane[l]) and then the
+        // lanes l = 0..7 left to right.  One accumulator at a time keeps only
+        // the eight lane sums live next to the cos|sin registers.
+        float lane[8];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            tmem_ld_32cols(taddr + c * 32, r);
+        for (int k = 0; k < 4; ++k) {
+            uint32_t r[4][8];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) tmem_ld_8cols(taddr + 32 * c + 8 * k, r[c]);
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                float2 f = make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
-                if (!p.fp32_epilogue) f = unpack_bf16x2(pack_bf16x2(f.x, f.y));
-                ss = fmaf(f.x, f.x, ss);       // squares of BF16 values are exact in FP32
-                ss = fmaf(f.y, f.y, ss);
+            for (int l = 0; l < 8; ++l) {
+                float acc = 0.f;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    float f = __uint_as_float(r[c][l]);
+                    if (!p.fp32_epilogue) f = bf16_round(f);
+                    const float sq = __fmul_rn(f, f);
+                    acc = c == 0 ? sq : __fadd_rn(acc, sq);
+                }
+                lane[l] = k == 0 ? acc : __fadd_rn(lane[l], acc);
             }
         }
+        float ss = lane[0];
+#pragma unroll
+        for (int l = 1; l < 8; ++l) ss = __fadd_rn(ss, lane[l]);
         const float eps = comp == 0 ? p.q_eps : p.k_eps;
-        scale = __frsqrt_rn(__fadd_rn(ss * (1.0f / 128.0f), eps));
+        scale = norm_scale(ss, eps);
     }
 
     // The staging boxes must have been read by the previous store.
@@ -673,7 +729,10 @@ __device__ void run_epilogue(const QkvParams& p, const Sched& sc, uint8_t* smem,
     uint8_t* box_lo = smem + OFF_STG + (warp - 2) * STAGING_PER_WARP;
     uint8_t* box_hi = box_lo + BOX_BYTES;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    wait_peers_entered(p, epoch);
+    // Parked in shared memory until the entry barrier needs it.
+    volatile int32_t* status_slot = reinterpret_cast<volatile int32_t*>(smem + OFF_MISC + 12);
+    if (threadIdx.x == 64) *status_slot = status_at_start(p);
+    bool entered = false;
 
     int local = 0;
     Walk walk = make_walk(p, sc);
@@ -701,6 +760,12 @@ __device__ void run_epilogue(const QkvParams& p, const Sched& sc, uint8_t* smem,
                             W_TFULL))
             break;
         tc_fence_after();
+        // Before the first store of this call: the entry barrier (its wait
+        // overlaps the first tile's main loop).  On failure nothing is stored.
+        if (!entered) {
+            if (!wait_peers_entered(p, epoch, abort_flag, kPair, *status_slot)) break;
+            entered = true;
+        }
         const uint32_t acc_addr = tmem_base + lane_addr + acc * BN;
         if (it.role != ROLE_EMIT) {
             // Stream-K partial of this CTA's 128 rows: [256 cols][128 rows] FP32, so a
@@ -791,6 +856,9 @@ __device__ void run_split_partial(const QkvParams& p, const Sched& sc, uint8_t* 
     const int lane = threadIdx.x & 31;
     const int quarter = warp & 3;
     const int m_blk = sc.first / p.num_n_blocks;
+    // Read now, used by the reduction's entry barrier (after the main loop).
+    if (threadIdx.x == 64) *reinterpret_cast<volatile int32_t*>(smem + OFF_MISC + 12) =
+        status_at_start(p);
     if (!fu_wait_parity(b.tfull, 0, abort_flag, p.timeout_ns, p.status, W_TFULL)) return;
     tc_fence_after();
     if (m_blk * BM + quarter * 32 >= p.L) return;          // no valid row in this warp
@@ -882,13 +950,38 @@ __device__ __forceinline__ void split_item_emit(const QkvParams& p, const float4
     const int dst_col = head_id % per_gpu;
     uint2 out = make_uint2(u0, u1);
     if (comp < 2) {
-        float ss = 0.f;
+        // The sum of squares in the order of torch's CPU reduction (as in
+        // emit_head): column j = 4 lane + e belongs to accumulator k =
+        // (lane / 2) % 4, eight-lane slot 4 (lane % 2) + e, step lane / 8.
+        // Every shuffle reads values that no earlier step of this sum changed.
+        float sq[4], acc[4], a[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) ss = fmaf(v[i], v[i], ss);
+        for (int e = 0; e < 4; ++e) acc[e] = sq[e] = __fmul_rn(v[e], v[e]);
 #pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        for (int step = 8; step <= 24; step += 8) {        // steps 1..3 into lanes 0..7
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                acc[e] = __fadd_rn(acc[e], __shfl_down_sync(0xffffffffu, sq[e], step));
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) a[e] = acc[e];
+#pragma unroll
+        for (int k = 2; k <= 6; k += 2) {                  // accumulators 1..3 into lanes 0, 1
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                a[e] = __fadd_rn(a[e], __shfl_down_sync(0xffffffffu, acc[e], k));
+        }
+        float hi[4];                                         // slots 4..7 (lane 1) to lane 0
+#pragma unroll
+        for (int e = 0; e < 4; ++e) hi[e] = __shfl_down_sync(0xffffffffu, a[e], 1);
+        float ss = a[0];
+#pragma unroll
+        for (int e = 1; e < 4; ++e) ss = __fadd_rn(ss, a[e]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ss = __fadd_rn(ss, hi[e]);
+        ss = __shfl_sync(0xffffffffu, ss, 0);
         const float eps = comp == 0 ? p.q_eps : p.k_eps;
-        const float scale = __frsqrt_rn(__fadd_rn(ss * (1.0f / 128.0f), eps));
+        const float scale = norm_scale(ss, eps);
         const float* g = gam + comp * 128 + 4 * lane;
         float n[4], partner[4];
 #pragma unroll
@@ -916,8 +1009,16 @@ __device__ __forceinline__ void split_item_emit(const QkvParams& p, const float4
 }
 
 __device__ void run_split_reduce(const QkvParams& p, const Sched& sc, uint8_t* smem,
-                                 const float* gam, uint32_t epoch) {
-    wait_peers_entered(p, epoch);
+                                 const float* gam, volatile int* abort_flag, uint32_t epoch) {
+    // The reduction reads every cluster CTA's partial: if any of them gave up
+    // (its partial is incomplete), this CTA stores nothing either.
+    if (threadIdx.x == 64) {
+        const uint32_t flag_addr = smem_u32(const_cast<int*>(abort_flag));
+        for (int r = 0; r < p.splits; ++r)
+            if (ld_cluster_u32(map_cluster_smem(flag_addr, r)) != 0) *abort_flag = 1;
+    }
+    const int32_t status_seen = *reinterpret_cast<volatile int32_t*>(smem + OFF_MISC + 12);
+    if (!wait_peers_entered(p, epoch, abort_flag, false, status_seen)) return;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int m_blk = sc.first / p.num_n_blocks;
@@ -1032,7 +1133,7 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
         // Every CTA of the cluster reaches both barriers on every path, so a
         // CTA that gave up on a wait cannot strand its peers here.
         cluster_sync_all();                 // partials visible cluster-wide
-        if (warp >= 2) run_split_reduce(p, sc, smem, gam, epoch);
+        if (warp >= 2) run_split_reduce(p, sc, smem, gam, abort_flag, epoch);
         cluster_sync_all();                 // peers are done reading this CTA's partial
     }
 
@@ -1052,6 +1153,10 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
             const bool any_abort = aborted || (old >> 16) != 0;
             *reinterpret_cast<volatile uint32_t*>(my_sync + FU_SYNC_COUNTER) = 0u;
             *reinterpret_cast<volatile uint32_t*>(my_sync + FU_SYNC_EPOCH) = epoch;
+            // A failed call of a group marks the operator failed: calls queued
+            // behind it skip their peer waits and stores.
+            if (any_abort && p.sp_size > 1)
+                *reinterpret_cast<volatile uint32_t*>(my_sync + FU_SYNC_FAILED) = 1u;
             if (!any_abort) {
                 if (p.sp_size == 1) {
                     st_release_gpu_u32(my_sync, epoch);
@@ -1241,7 +1346,7 @@ extern "C" int fu_qkv_create(const fu_qkv_topology* topo, fu_qkv_ctx** out) {
     }
     cudaSetDevice(prev);
     ctx->topo = *topo;
-    if (ctx->topo.timeout_ns == 0) ctx->topo.timeout_ns = 5000000000ull;
+    if (ctx->topo.timeout_ns == 0) ctx->topo.timeout_ns = FU_DEFAULT_TIMEOUT_NS;
     ctx->sm_count = sms;
     std::memset(&ctx->params, 0, sizeof(ctx->params));
     *out = ctx;
@@ -1480,7 +1585,6 @@ struct NoallocDevice {
     char message[256] = {0};
     uint32_t* scratch = nullptr;     // device address of g_noalloc_scratch
     int sm_count = 0;
-    uint32_t epoch = 0;
 };
 static NoallocDevice g_noalloc_devices[kNoallocMaxDevices];
 
@@ -1525,9 +1629,12 @@ extern "C" int fu_qkv_forward_noalloc(int device, const void* x, const void* w,
                          "local_tokens %lld outside [1, %d], the largest count the kernel's "
                          "32-bit row indices and the fixed scratch serve",
                          static_cast<long long>(L), FU_NOALLOC_MAX_TOKENS);
-    if (hidden_size <= 0 || hidden_size % 64 || hidden_size > (int64_t(1) << 30))
+    if (hidden_size <= 0 || hidden_size % 64)
         return set_error(FU_ERR_INVALID, "hidden_size %lld must be a positive multiple of 64",
                          static_cast<long long>(hidden_size));
+    if (hidden_size > (int64_t(1) << 30))
+        return set_error(FU_ERR_INVALID, "hidden_size %lld exceeds 2^30, the kernel's 32-bit "
+                         "column indices", static_cast<long long>(hidden_size));
     if (q_heads <= 0 || kv_heads <= 0 || q_heads > 4096 || kv_heads > 4096)
         return set_error(FU_ERR_INVALID, "head counts (%d, %d) out of range", q_heads, kv_heads);
     if (!x || !w || !positions || !q_gamma || !k_gamma || !rope || !q_out || !k_out || !v_out)
@@ -1598,7 +1705,7 @@ extern "C" int fu_qkv_forward_noalloc(int device, const void* x, const void* w,
     p.gemm_out = nullptr;
     p.sync[0] = st.scratch;
     p.status = status;
-    p.timeout_ns = 5000000000ull;
+    p.timeout_ns = FU_DEFAULT_TIMEOUT_NS;
     p.L = static_cast<int32_t>(L);
     p.H = static_cast<int32_t>(hidden_size);
     p.N = static_cast<int32_t>(N);
@@ -1620,7 +1727,6 @@ extern "C" int fu_qkv_forward_noalloc(int device, const void* x, const void* w,
     p.k_eps = static_cast<float>(k_epsilon);
     // The kernel advances the epoch word of the scratch itself; only the
     // completion counter must start at zero.
-    ++st.epoch;
     p.wait_peers = 1u;
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -49,12 +49,18 @@ extern "C" {
  *   [FU_SYNC_EPOCH]           this rank's epoch: the number of calls made,
  *                             advanced by the kernel itself, so captured CUDA
  *                             graphs replay with fresh epochs
+ *   [FU_SYNC_FAILED]          nonzero once a call of this operator gave up a
+ *                             wait (sp_size > 1): later calls that start while
+ *                             it is set store nothing and wait for nothing
+ *                             (local use only; cleared with the counter when
+ *                             the caller clears the error)
  * Calls of one SP group advance in lockstep: every rank makes the same calls.
  */
 #define FU_SYNC_WORDS 64
 #define FU_SYNC_ENTRY 8
 #define FU_SYNC_COUNTER 32
 #define FU_SYNC_EPOCH 33
+#define FU_SYNC_FAILED 35
 
 enum fu_error {
     FU_OK = 0,
@@ -72,6 +78,14 @@ enum fu_device_status {
     FU_STATUS_PEER_TIMEOUT = 2,
     FU_STATUS_POSITION_RANGE = 3
 };
+
+/* Default bound on a device-side wait: 30 s, long enough for ranks whose
+ * calls start seconds apart (start-up, a garbage-collection pause).  A wait
+ * that gives up records the failure in the status word and in the sync
+ * block's FU_SYNC_FAILED word; a call that starts with that word set (queued
+ * behind a failed one) stores nothing and waits for nothing, so one failure
+ * costs one timeout, not one per queued call. */
+#define FU_DEFAULT_TIMEOUT_NS 30000000000ull
 
 /* Flags for fu_qkv_forward. */
 #define FU_FWD_NO_PEER_WAIT 1u  /* publish entry/exit flags but wait for no peer */
@@ -150,7 +164,7 @@ typedef struct fu_qkv_topology {
     int32_t* status;         /* device pointer of a status word, may be NULL */
     int32_t* status_host;    /* host view of the same word (fu_status_alloc), may be NULL;
                                 fu_qkv_forward refuses to launch while it is nonzero */
-    uint64_t timeout_ns;     /* bound on every device-side wait; 0 = 5 s */
+    uint64_t timeout_ns;     /* bound on every device-side wait; 0 = FU_DEFAULT_TIMEOUT_NS */
 } fu_qkv_topology;
 
 /* Create the per-rank operator state (tensor-map caches, epoch counter).
@@ -265,7 +279,7 @@ typedef struct fu_oproj_topology {
     uint32_t* sync[FU_MAX_SP];
     int32_t* status;          /* device pointer of a status word, may be NULL */
     int32_t* status_host;     /* host view of the same word, may be NULL */
-    uint64_t timeout_ns;      /* bound on every device-side wait; 0 = 5 s */
+    uint64_t timeout_ns;      /* bound on every device-side wait; 0 = FU_DEFAULT_TIMEOUT_NS */
 } fu_oproj_topology;
 
 /* Words of an o-projection sync block for calls of up to max_local_tokens. */

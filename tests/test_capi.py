@@ -138,12 +138,12 @@ int main(void) {{
 
 
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="no host C compiler")
-def test_integration_c_example_compiles(tmp_path):
-    """The C example in INTEGRATION.md compiles against the header as written."""
-    text = (HEADER.parent.parent / "INTEGRATION.md").read_text()
-    blocks = re.findall(r"```c\n(.*?)```", text, re.S)
-    assert blocks, "no C example found"
+def test_c_example_layer_compiles(tmp_path):
+    """The C example caller (one layer: forward exchange, then the output
+    side) compiles against the header without warnings."""
+    example = Path(__file__).resolve().parent / "c_example_layer.c"
     src = tmp_path / "example.c"
-    src.write_text(blocks[0].replace('#include "flash_ulysses_b200.h"', f'#include "{HEADER}"'))
+    src.write_text(example.read_text().replace('#include "flash_ulysses_b200.h"',
+                                               f'#include "{HEADER}"'))
     subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", "-c", str(src),
                     "-o", str(tmp_path / "example.o")], check=True)

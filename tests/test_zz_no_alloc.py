@@ -14,9 +14,10 @@ import ctypes
 import pytest
 import torch
 
-from emulation import EmulatedGroup, isclose_stats, to_device
+from emulation import EmulatedGroup, to_device
 from flash_ulysses_b200 import _C
 from flash_ulysses_b200.workloads import make_parameters, make_rank_inputs
+from oracle import ulysses_oracle as oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -25,15 +26,18 @@ H, QH, KVH = 4096, 32, 8
 
 def existing_entry_point(x, pos, params, tokens):
     """Outputs of the context-based entry point (fu_qkv_forward), world of one,
-    on the same kernel variant (one CTA per tile over the full reduction) that
-    the allocation-free entry point runs."""
+    pinned to the kernel variant the allocation-free entry point runs (one CTA
+    per 128 x 256 tile over the full reduction), and that call's BF16
+    projection (test instrumentation)."""
     group = EmulatedGroup(sp_size=1, hidden_size=H, q_heads=QH, kv_heads=KVH,
                           max_local_tokens=tokens)
     try:
-        group.run([x], [pos], [params], flags=_C.FU_FWD_SPLITS(1))
+        proj = torch.empty(tokens, (QH + 2 * KVH) * 128, dtype=torch.bfloat16, device=x.device)
+        group.run([x], [pos], [params], gemm_outs=[proj],
+                  flags=_C.FU_FWD_NO_PEER_WAIT | _C.FU_FWD_SPLITS(1) | _C.FU_FWD_SINGLE)
         torch.cuda.synchronize()
         assert group.status.value == 0
-        return tuple(t.clone() for t in group.outputs(tokens)[0])
+        return tuple(t.clone() for t in group.outputs(tokens)[0]), proj
     finally:
         group.close()
 
@@ -72,10 +76,22 @@ def test_noalloc_matches_existing_entry_point_on_two_calls():
         assert int(status.item()) == 0
         results.append([o.clone() for o in outs])
     for (x, pos, params, tokens), got in zip(cases, results):
-        want = existing_entry_point(x, pos, params, tokens)
+        want, proj = existing_entry_point(x, pos, params, tokens)
+        # Same kernel variant, same inputs: the same bits.
         for g, w, name in zip(got, want, "QKV"):
-            bad, err = isclose_stats(g, w, atol=0.01, rtol=0.01)
-            assert bad == 0, f"{name}: {bad} elements differ beyond 0.01/0.01 (max {err})"
+            assert torch.equal(g.view(torch.int16), w.view(torch.int16)), name
+        # And that variant against the CPU oracle: projection within one BF16
+        # ulp of x @ W, epilogue bit for bit on that projection.
+        cpu = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in params.items()}
+        xs, ps = [x.cpu()], [pos.cpu()]
+        ref = oracle.project(xs[0], cpu["qkv_weight"]).float()
+        a = proj.cpu().float()
+        assert bool(((a - ref).abs() <= torch.maximum(a.abs(), ref.abs()) * 2.0 ** -7 + 1e-4)
+                    .all())
+        topo = oracle.Topology(1, 1, QH, KVH, H)
+        exp = oracle.simulate_world(topo, xs, ps, [cpu], projections=[proj.cpu()])[0]
+        for g, e, name in zip(got, exp, "QKV"):
+            assert torch.equal(g.cpu().view(torch.int16), e.view(torch.int16)), name
 
 
 def test_noalloc_rejects_oversized_and_bad_arguments():
