@@ -329,8 +329,11 @@ def _cpu_rank_worker(rank, sp, port, shape, tokens, steps, warmup, budget_s, thr
     import datetime
 
     torch.set_num_threads(threads)
-    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
-                            world_size=sp, timeout=datetime.timedelta(seconds=600))
+    # An explicit store: under torch.distributed.run the inherited environment
+    # would otherwise point the rendezvous at the launcher's agent store.
+    timeout = datetime.timedelta(seconds=600)
+    store = dist.TCPStore("127.0.0.1", port, sp, rank == 0, timeout=timeout)
+    dist.init_process_group("gloo", store=store, rank=rank, world_size=sp, timeout=timeout)
     from flash_ulysses_b200.workloads import make_parameters, make_rank_inputs
     from oracle import ulysses_oracle as oracle
 
