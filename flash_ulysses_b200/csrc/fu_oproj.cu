@@ -499,12 +499,9 @@ oproj_exchange_kernel(const __grid_constant__ OprojParams p) {
     uint32_t* my_sync = p.sync[p.sp_rank];
     const bool leader = !kPair || cluster_ctarank() == 0;
 
+    // Prologue: shared memory, TMEM and parameters only (it may overlap the
+    // previous kernel of the stream under a programmatic dependent launch).
     if (threadIdx.x == 0) {
-        const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my_sync + FU_SYNC_EPOCH) + 1;
-        *epoch_slot = epoch;
-        if (blockIdx.x == 0 && p.sp_size > 1 && p.do_gather)
-            for (int d = 0; d < p.sp_size; ++d)
-                st_release_sys_u32(p.sync[d] + FU_SYNC_ENTRY + p.sp_rank, epoch);
         for (int s = 0; s < MAX_STAGES; ++s) {
             mbar_init(b.full + 8 * s, 1);
             mbar_init(b.empty + 8 * s, 1);
@@ -530,6 +527,18 @@ oproj_exchange_kernel(const __grid_constant__ OprojParams p) {
             tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
             tmem_relinquish();
         }
+    }
+    // Global memory from here on: the previous kernel of the stream is done.
+    grid_dependency_wait();
+    grid_launch_dependents();
+    if (threadIdx.x == 0) {
+        const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my_sync + FU_SYNC_EPOCH) + 1;
+        *epoch_slot = epoch;
+        // "Entered e" carries no data (this rank's earlier reads of G are
+        // complete): posted stores.
+        if (blockIdx.x == 0 && p.sp_size > 1 && p.do_gather)
+            for (int d = 0; d < p.sp_size; ++d)
+                st_relaxed_sys_u32(p.sync[d] + FU_SYNC_ENTRY + p.sp_rank, epoch);
     }
     tc_fence_before();
     __syncthreads();
@@ -803,26 +812,29 @@ extern "C" int fu_oproj_forward(fu_oproj_ctx* ctx, const void* attn, const void*
     int prev = 0;
     cudaGetDevice(&prev);
     if (prev != t.device) cudaSetDevice(t.device);
-    cudaError_t e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(oproj::NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = oproj::SMEM_ALLOC;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attrs[2];
+    int n_attrs = 0;
     if (pair) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(grid, 1, 1);
-        cfg.blockDim = dim3(oproj::NUM_THREADS, 1, 1);
-        cfg.dynamicSmemBytes = oproj::SMEM_ALLOC;
-        cfg.stream = static_cast<cudaStream_t>(stream);
-        cudaLaunchAttribute attr;
-        attr.id = cudaLaunchAttributeClusterDimension;
-        attr.val.clusterDim.x = 2;
-        attr.val.clusterDim.y = 1;
-        attr.val.clusterDim.z = 1;
-        cfg.attrs = &attr;
-        cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, oproj::oproj_exchange_kernel<true>, p);
-    } else {
-        oproj::oproj_exchange_kernel<false><<<grid, oproj::NUM_THREADS, oproj::SMEM_ALLOC,
-                                              static_cast<cudaStream_t>(stream)>>>(p);
-        e = cudaGetLastError();
+        attrs[n_attrs].id = cudaLaunchAttributeClusterDimension;
+        attrs[n_attrs].val.clusterDim.x = 2;
+        attrs[n_attrs].val.clusterDim.y = 1;
+        attrs[n_attrs].val.clusterDim.z = 1;
+        ++n_attrs;
     }
+    if ((flags & FU_FWD_NO_PDL) == 0) {      // as for fu_qkv_forward
+        attrs[n_attrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attrs[n_attrs].val.programmaticStreamSerializationAllowed = 1;
+        ++n_attrs;
+    }
+    cfg.attrs = attrs;
+    cfg.numAttrs = n_attrs;
+    cudaError_t e = pair ? cudaLaunchKernelEx(&cfg, oproj::oproj_exchange_kernel<true>, p)
+                         : cudaLaunchKernelEx(&cfg, oproj::oproj_exchange_kernel<false>, p);
     if (prev != t.device) cudaSetDevice(prev);
     if (e != cudaSuccess) return set_error(FU_ERR_CUDA, "launch failed: %s", cudaGetErrorString(e));
     ++ctx->calls;

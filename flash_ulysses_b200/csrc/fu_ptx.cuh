@@ -24,6 +24,24 @@ __device__ __forceinline__ bool elect_lane0() {
     return (threadIdx.x & 31) == 0;
 }
 
+// ---------------------------------------------------------------- dependent launch
+// Programmatic dependent launch (the launch attribute
+// cudaLaunchAttributeProgrammaticStreamSerialization): the kernel may start
+// while the previous kernel of its stream is still running.  Before
+// grid_dependency_wait() a thread may touch only its CTA's shared memory,
+// TMEM and the kernel parameters; afterwards every write of the previous
+// kernel is visible.  Without the attribute both are no-ops.
+__device__ __forceinline__ void grid_dependency_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Lets the next kernel of the stream (if launched with the attribute) start
+// its own prologue; it still waits for this grid's completion before it
+// reads global memory.
+__device__ __forceinline__ void grid_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
@@ -322,6 +340,12 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16_f32(int m, int n, bool a_
 // ---------------------------------------------------------------- flags
 __device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// A posted flag store to (possibly) a peer's memory; ordering with earlier
+// writes, where needed, comes from one fence before a batch of these.
+__device__ __forceinline__ void st_relaxed_sys_u32(uint32_t* p, uint32_t v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {

@@ -317,11 +317,11 @@ struct Bars {
           tempty(base + 16 * MAX_STAGES + 16), mma_done(base + 16 * MAX_STAGES + 32) {}
 };
 
-// Whether an earlier call of this operator gave up a wait (the sticky
-// FU_SYNC_FAILED word of this rank's own sync block, in device memory: a read
+// Whether an earlier call of this operator gave up a wait: the sticky
+// FU_SYNC_FAILED word of this rank's own sync block, in device memory (a read
 // of the host-mapped status word from every CTA would cost a serialised
-// host-memory round trip each).  Read early by the thread that runs the entry
-// barrier, so the read overlaps the main loop.
+// host-memory round trip each).  Read by the thread that runs the entry
+// barrier.
 __device__ __forceinline__ int32_t status_at_start(const QkvParams& p) {
     if (threadIdx.x != 64 || p.sp_size == 1) return 0;
     return static_cast<int32_t>(
@@ -729,10 +729,8 @@ __device__ void run_epilogue(const QkvParams& p, const Sched& sc, uint8_t* smem,
     uint8_t* box_lo = smem + OFF_STG + (warp - 2) * STAGING_PER_WARP;
     uint8_t* box_hi = box_lo + BOX_BYTES;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    // Parked in shared memory until the entry barrier needs it.
-    volatile int32_t* status_slot = reinterpret_cast<volatile int32_t*>(smem + OFF_MISC + 12);
-    if (threadIdx.x == 64) *status_slot = status_at_start(p);
-    bool entered = false;
+    // Every epilogue thread reaches this barrier; on failure nothing is stored.
+    if (!wait_peers_entered(p, epoch, abort_flag, kPair, status_at_start(p))) return;
 
     int local = 0;
     Walk walk = make_walk(p, sc);
@@ -760,12 +758,6 @@ __device__ void run_epilogue(const QkvParams& p, const Sched& sc, uint8_t* smem,
                             W_TFULL))
             break;
         tc_fence_after();
-        // Before the first store of this call: the entry barrier (its wait
-        // overlaps the first tile's main loop).  On failure nothing is stored.
-        if (!entered) {
-            if (!wait_peers_entered(p, epoch, abort_flag, kPair, *status_slot)) break;
-            entered = true;
-        }
         const uint32_t acc_addr = tmem_base + lane_addr + acc * BN;
         if (it.role != ROLE_EMIT) {
             // Stream-K partial of this CTA's 128 rows: [256 cols][128 rows] FP32, so a
@@ -1063,13 +1055,9 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
 
     uint32_t* my_sync = p.sync[p.sp_rank];
     uint32_t* epoch_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC + 8);
+    // Prologue: shared memory, TMEM and parameters only, so that under a
+    // programmatic dependent launch it overlaps the previous kernel's tail.
     if (threadIdx.x == 0) {
-        // This call's epoch: one past the last call's (the kernel advances it).
-        const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my_sync + FU_SYNC_EPOCH) + 1;
-        *epoch_slot = epoch;
-        if (blockIdx.x == 0 && p.sp_size > 1)
-            for (int d = 0; d < p.sp_size; ++d)
-                st_release_sys_u32(p.sync[d] + FU_SYNC_ENTRY + p.sp_rank, epoch);
         for (int s = 0; s < R::STAGES; ++s) {
             mbar_init(b.full + 8 * s, 1);
             mbar_init(b.empty + 8 * s, 1);
@@ -1085,8 +1073,6 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
         tma_prefetch_desc(&p.tm_x);
         tma_prefetch_desc(&p.tm_w);
     }
-    for (int i = threadIdx.x; i < 256; i += NUM_THREADS)
-        gam[i] = i < 128 ? p.q_gamma[i] : p.k_gamma[i - 128];
     if (warp == 1) {
         if (kPair) {
             tmem_alloc_pair(smem_u32(tmem_holder), TMEM_COLS);
@@ -1095,6 +1081,20 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
             tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
             tmem_relinquish();
         }
+    }
+    // Global memory from here on: the previous kernel of the stream is done.
+    grid_dependency_wait();
+    grid_launch_dependents();
+    if (threadIdx.x == 0) {
+        // This call's epoch: one past the last call's (the kernel advances it).
+        const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(my_sync + FU_SYNC_EPOCH) + 1;
+        *epoch_slot = epoch;
+        // "Entered e": this rank's stream has finished everything before this
+        // call, so its earlier reads of the receive buffers are complete; the
+        // flag carries no data, so posted (relaxed) stores suffice.
+        if (blockIdx.x == 0 && p.sp_size > 1)
+            for (int d = 0; d < p.sp_size; ++d)
+                st_relaxed_sys_u32(p.sync[d] + FU_SYNC_ENTRY + p.sp_rank, epoch);
     }
     tc_fence_before();
     __syncthreads();
@@ -1111,10 +1111,16 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
         if (lane == 0 && (!kPair || sc.rank == 0))
             run_mma<kPair>(p, sc, smem, tmem_base, b, abort_flag);
         __syncwarp();
-    } else if (split_mode) {
-        run_split_partial(p, sc, smem, tmem_base, b, abort_flag);
     } else {
-        run_epilogue<kPair>(p, sc, smem, tmem_base, b, gam, abort_flag, epoch);
+        // The norm weights, staged by the epilogue warps (off the producer's
+        // start-up path); the entry barrier's named barrier, or the split
+        // reduction's cluster barrier, orders them before their first use.
+        for (int i = threadIdx.x - 64; i < 256; i += NUM_EPI_THREADS)
+            gam[i] = i < 128 ? p.q_gamma[i] : p.k_gamma[i - 128];
+        if (split_mode)
+            run_split_partial(p, sc, smem, tmem_base, b, abort_flag);
+        else
+            run_epilogue<kPair>(p, sc, smem, tmem_base, b, gam, abort_flag, epoch);
     }
 
     tc_fence_before();
@@ -1161,8 +1167,12 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
                 if (p.sp_size == 1) {
                     st_release_gpu_u32(my_sync, epoch);
                 } else {
+                    // One system-scope fence orders every counted CTA's stores
+                    // (acquired through the counter) before all the flags; the
+                    // flags themselves are posted stores.
+                    fence_acq_rel_sys();
                     for (int d = 0; d < p.sp_size; ++d)
-                        st_release_sys_u32(p.sync[d] + p.sp_rank, epoch);
+                        st_relaxed_sys_u32(p.sync[d] + p.sp_rank, epoch);
                     if (p.wait_peers) {
                         const uint64_t t0 = globaltimer_ns();
                         for (int s = 0; s < p.sp_size; ++s) {
@@ -1531,27 +1541,32 @@ extern "C" int fu_qkv_forward(fu_qkv_ctx* ctx, const void* x, const void* w,
     int prev = 0;
     cudaGetDevice(&prev);
     if (prev != t.device) cudaSetDevice(t.device);
-    cudaError_t e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = SMEM_ALLOC;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attrs[2];
+    int n_attrs = 0;
     if (pair || p.splits > 1) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(grid, 1, 1);
-        cfg.blockDim = dim3(NUM_THREADS, 1, 1);
-        cfg.dynamicSmemBytes = SMEM_ALLOC;
-        cfg.stream = static_cast<cudaStream_t>(stream);
-        cudaLaunchAttribute attr;
-        attr.id = cudaLaunchAttributeClusterDimension;
-        attr.val.clusterDim.x = pair ? 2 : p.splits;
-        attr.val.clusterDim.y = 1;
-        attr.val.clusterDim.z = 1;
-        cfg.attrs = &attr;
-        cfg.numAttrs = 1;
-        e = pair ? cudaLaunchKernelEx(&cfg, fused_qkv_exchange_kernel<true>, p)
-                 : cudaLaunchKernelEx(&cfg, fused_qkv_exchange_kernel<false>, p);
-    } else {
-        fused_qkv_exchange_kernel<false><<<grid, NUM_THREADS, SMEM_ALLOC,
-                                           static_cast<cudaStream_t>(stream)>>>(p);
-        e = cudaGetLastError();
+        attrs[n_attrs].id = cudaLaunchAttributeClusterDimension;
+        attrs[n_attrs].val.clusterDim.x = pair ? 2 : p.splits;
+        attrs[n_attrs].val.clusterDim.y = 1;
+        attrs[n_attrs].val.clusterDim.z = 1;
+        ++n_attrs;
     }
+    if ((flags & FU_FWD_NO_PDL) == 0) {
+        // The prologue (barriers, TMEM, descriptor prefetch) may overlap the
+        // previous kernel of the stream; the kernel waits for it before it
+        // touches global memory.
+        attrs[n_attrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attrs[n_attrs].val.programmaticStreamSerializationAllowed = 1;
+        ++n_attrs;
+    }
+    cfg.attrs = attrs;
+    cfg.numAttrs = n_attrs;
+    cudaError_t e = pair ? cudaLaunchKernelEx(&cfg, fused_qkv_exchange_kernel<true>, p)
+                         : cudaLaunchKernelEx(&cfg, fused_qkv_exchange_kernel<false>, p);
     if (prev != t.device) cudaSetDevice(prev);
     if (e != cudaSuccess) return set_error(FU_ERR_CUDA, "launch failed: %s", cudaGetErrorString(e));
     return FU_OK;

@@ -115,6 +115,13 @@ enum fu_device_status {
  * partial last round of the data-parallel grid runs faster per tile than a
  * full one, which leaves stream-K slower at every measured size. */
 #define FU_FWD_STREAMK (1u << 16)
+/* Launch without programmatic dependent launch.  By default the kernel is
+ * launched with cudaLaunchAttributeProgrammaticStreamSerialization: its
+ * prologue (barrier set-up, TMEM allocation) may run while the previous
+ * kernel of the stream finishes, and it reads or writes no global memory
+ * before that kernel has completed; it also lets the next such kernel of the
+ * stream start its prologue early.  Results are the same either way. */
+#define FU_FWD_NO_PDL (1u << 17)
 
 FU_API const char* fu_last_error(void);
 FU_API int fu_version(void);
@@ -288,7 +295,8 @@ FU_API int fu_oproj_create(const fu_oproj_topology* topo, fu_oproj_ctx** out);
 FU_API int fu_oproj_destroy(fu_oproj_ctx* ctx);
 
 /* One call, one launch on `stream` (flags: FU_FWD_NO_PEER_WAIT, FU_FWD_SINGLE /
- * FU_FWD_PAIR to force the GEMM variant, FU_OPROJ_GATHER_ONLY / FU_OPROJ_GEMM_ONLY):
+ * FU_FWD_PAIR to force the GEMM variant, FU_FWD_NO_PDL, FU_OPROJ_GATHER_ONLY /
+ * FU_OPROJ_GEMM_ONLY):
  *   attn   BF16 [S * local_tokens, q_heads/S * 128], this rank's attention output
  *   w_o    BF16 [H, q_heads * 128]
  *   out    BF16 [local_tokens, H]
