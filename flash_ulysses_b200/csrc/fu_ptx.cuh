@@ -175,6 +175,10 @@ __device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
     return v;
 }
 
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // Wait until every committed bulk store has completed (writes performed).
 __device__ __forceinline__ void bulk_wait_all() {
     asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");

@@ -851,6 +851,29 @@ __device__ void run_split_partial(const QkvParams& p, const Sched& sc, uint8_t* 
     // Read now, used by the reduction's entry barrier (after the main loop).
     if (threadIdx.x == 64) *reinterpret_cast<volatile int32_t*>(smem + OFF_MISC + 12) =
         status_at_start(p);
+    // While the tensor cores work: this tile's token positions, validated, as
+    // RoPE row indices in shared memory (the staging area is unused in split
+    // mode), and the RoPE rows prefetched into L2, so that the reduction's
+    // per-item chain is one L2 hit instead of two dependent loads.
+    {
+        const int row = threadIdx.x - 64;
+        const int m = m_blk * BM + row;
+        int32_t rope_row = 0;
+        if (m < p.L) {
+            const int64_t pos = __ldg(p.positions + m);
+            if (pos < 0 || pos >= p.rope_rows)
+                report_status(p.status, FU_DEV_POSITION_RANGE, 0);
+            else
+                rope_row = static_cast<int32_t>(pos);
+            const int n_blk = sc.first % p.num_n_blocks;
+            if (n_blk * 2 < p.q_heads + p.kv_heads) {          // a Q/K head in this tile
+                const float* r = p.rope + static_cast<int64_t>(rope_row) * 128;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) prefetch_l2(r + 32 * c);
+            }
+        }
+        reinterpret_cast<int32_t*>(smem + OFF_STG)[row] = rope_row;
+    }
     if (!fu_wait_parity(b.tfull, 0, abort_flag, p.timeout_ns, p.status, W_TFULL)) return;
     tc_fence_after();
     if (m_blk * BM + quarter * 32 >= p.L) return;          // no valid row in this warp
@@ -876,20 +899,6 @@ __device__ void run_split_partial(const QkvParams& p, const Sched& sc, uint8_t* 
 // sums them in rank order (deterministic).  The RMSNorm sum is a warp
 // reduction, the NeoX partner of lane l is lane l^16, and the row leaves as
 // one coalesced 256-byte store into the destination rank's receive buffer.
-__device__ __forceinline__ void split_item_load(const QkvParams& p, uint32_t local, int splits,
-                                                float4& t) {
-    float4 v[FU_MAX_SP];
-#pragma unroll
-    for (int s = 0; s < FU_MAX_SP; ++s)
-        if (s < splits) v[s] = ld_cluster_f32x4(map_cluster_smem(local, s));
-    t = v[0];
-#pragma unroll
-    for (int s = 1; s < FU_MAX_SP; ++s)
-        if (s < splits) {
-            t.x += v[s].x; t.y += v[s].y; t.z += v[s].z; t.w += v[s].w;
-        }
-}
-
 // cos|sin of columns 4l..4l+3 (mod 64) at token row m's position, for a Q/K
 // head (V heads are not rotated); issued before the partial sums are read so
 // the two latencies overlap.
@@ -897,18 +906,14 @@ struct SplitRope {
     float4 cs, sn;
 };
 
-__device__ __forceinline__ SplitRope split_item_rope(const QkvParams& p, int m, int h, int lane) {
+__device__ __forceinline__ SplitRope split_item_rope(const QkvParams& p, const int32_t* rope_rows,
+                                                    int row, int h, int lane) {
     SplitRope r;
     r.cs = r.sn = make_float4(0.f, 0.f, 0.f, 0.f);
     if (h < p.q_heads + p.kv_heads) {
-        int64_t pos = __ldg(p.positions + m);
-        if (pos < 0 || pos >= p.rope_rows) {
-            report_status(p.status, FU_DEV_POSITION_RANGE, 0);
-            pos = 0;
-        }
-        const int j0 = 4 * (lane & 15);
-        r.cs = __ldg(reinterpret_cast<const float4*>(p.rope + pos * 128 + j0));
-        r.sn = __ldg(reinterpret_cast<const float4*>(p.rope + pos * 128 + 64 + j0));
+        const float* base = p.rope + static_cast<int64_t>(rope_rows[row]) * 128 + 4 * (lane & 15);
+        r.cs = __ldg(reinterpret_cast<const float4*>(base));
+        r.sn = __ldg(reinterpret_cast<const float4*>(base + 64));
     }
     return r;
 }
@@ -1003,11 +1008,18 @@ __device__ __forceinline__ void split_item_emit(const QkvParams& p, const float4
 __device__ void run_split_reduce(const QkvParams& p, const Sched& sc, uint8_t* smem,
                                  const float* gam, volatile int* abort_flag, uint32_t epoch) {
     // The reduction reads every cluster CTA's partial: if any of them gave up
-    // (its partial is incomplete), this CTA stores nothing either.
+    // (its partial is incomplete), this CTA stores nothing either.  All flags
+    // are requested before any is examined, so the reads overlap.
     if (threadIdx.x == 64) {
         const uint32_t flag_addr = smem_u32(const_cast<int*>(abort_flag));
-        for (int r = 0; r < p.splits; ++r)
-            if (ld_cluster_u32(map_cluster_smem(flag_addr, r)) != 0) *abort_flag = 1;
+        uint32_t flags[FU_MAX_SP];
+#pragma unroll
+        for (int r = 0; r < FU_MAX_SP; ++r)
+            flags[r] = r < p.splits ? ld_cluster_u32(map_cluster_smem(flag_addr, r)) : 0u;
+        uint32_t any = 0;
+#pragma unroll
+        for (int r = 0; r < FU_MAX_SP; ++r) any |= flags[r];
+        if (any) *abort_flag = 1;
     }
     const int32_t status_seen = *reinterpret_cast<volatile int32_t*>(smem + OFF_MISC + 12);
     if (!wait_peers_entered(p, epoch, abort_flag, false, status_seen)) return;
@@ -1020,19 +1032,60 @@ __device__ void run_split_reduce(const QkvParams& p, const Sched& sc, uint8_t* s
     const int items = rows * heads_here;
     const int workers = 4 * p.splits;
     const uint32_t part = smem_u32(smem + OFF_A);
-    // Item i: row i / heads_here, head slot i % heads_here.
-    for (int i0 = (warp - 2) * p.splits + sc.split; i0 < items; i0 += 2 * workers) {
-        const int i1 = i0 + workers;
-        const bool has1 = i1 < items;
-        const int r0 = i0 / heads_here, hs0 = i0 % heads_here;
-        const int r1 = has1 ? i1 / heads_here : r0, hs1 = has1 ? i1 % heads_here : hs0;
-        const SplitRope rope0 = split_item_rope(p, m_blk * BM + r0, n_blk * 2 + hs0, lane);
-        const SplitRope rope1 = split_item_rope(p, m_blk * BM + r1, n_blk * 2 + hs1, lane);
-        float4 a0, a1;
-        split_item_load(p, part + r0 * PART_STRIDE + (hs0 * 128 + 4 * lane) * 4, p.splits, a0);
-        split_item_load(p, part + r1 * PART_STRIDE + (hs1 * 128 + 4 * lane) * 4, p.splits, a1);
-        split_item_emit(p, a0, m_blk * BM + r0, n_blk * 2 + hs0, gam, lane, rope0);
-        if (has1) split_item_emit(p, a1, m_blk * BM + r1, n_blk * 2 + hs1, gam, lane, rope1);
+    const int32_t* rope_rows = reinterpret_cast<const int32_t*>(smem + OFF_STG);
+    // Item i: row i / heads_here, head slot i % heads_here.  A warp takes two
+    // items per step (i0 and i0 + workers).  Each step first sums the partials
+    // requested by the previous step (in rank order: deterministic), then
+    // requests the next step's partials over distributed shared memory and its
+    // RoPE values, and only then normalises, rotates and stores the current
+    // items, so the remote reads of one step overlap the arithmetic of the
+    // step before.
+    struct Raw {
+        float4 v[2][FU_MAX_SP];
+        SplitRope rope[2];
+    };
+    auto request = [&](int i0, Raw& raw) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int i = min(i0 + k * workers, items - 1);
+            raw.rope[k] = split_item_rope(p, rope_rows, i / heads_here,
+                                          n_blk * 2 + i % heads_here, lane);
+        }
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int i = min(i0 + k * workers, items - 1);
+            const uint32_t local = part + (i / heads_here) * PART_STRIDE +
+                                   ((i % heads_here) * 128 + 4 * lane) * 4;
+#pragma unroll
+            for (int r = 0; r < FU_MAX_SP; ++r)
+                if (r < p.splits) raw.v[k][r] = ld_cluster_f32x4(map_cluster_smem(local, r));
+        }
+    };
+    const int first = (warp - 2) * p.splits + sc.split;
+    Raw raw;
+    if (first < items) request(first, raw);
+    for (int i0 = first; i0 < items; i0 += 2 * workers) {
+        float4 acc[2];
+        SplitRope rope[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            acc[k] = raw.v[k][0];
+#pragma unroll
+            for (int r = 1; r < FU_MAX_SP; ++r)
+                if (r < p.splits) {
+                    acc[k].x += raw.v[k][r].x; acc[k].y += raw.v[k][r].y;
+                    acc[k].z += raw.v[k][r].z; acc[k].w += raw.v[k][r].w;
+                }
+            rope[k] = raw.rope[k];
+        }
+        if (i0 + 2 * workers < items) request(i0 + 2 * workers, raw);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int i = i0 + k * workers;
+            if (i < items)
+                split_item_emit(p, acc[k], m_blk * BM + i / heads_here,
+                                n_blk * 2 + i % heads_here, gam, lane, rope[k]);
+        }
     }
 }
 
