@@ -56,6 +56,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--shape", choices=sorted(SHAPES), default="c1",
                     help="per-rank model shape (default c1: H=4096, 32/8 heads)")
+    ap.add_argument("--nvlink-capture", action="store_true",
+                    help="one process drives an SP group of two on GPUs 0 and 1 without peer "
+                         "waits, so that a one-GPU ncu capture of rank 0's launch sees the "
+                         "exchange's NVLink traffic (prints one JSON line)")
     args = ap.parse_args()
     global HIDDEN, Q_HEADS, KV_HEADS, MAX_POS
     HIDDEN, Q_HEADS, KV_HEADS, MAX_POS = SHAPES[args.shape]
@@ -86,6 +90,10 @@ NVLINK_GBS = 770.0      # measured peer copy per direction on this pool (900 nom
 # profiles/fused_qkv_exchange_c1shape.md).  Keyed by tokens per rank.
 PROFILED_TRAFFIC = {4096: 186390016.0}
 PROFILED_TRAFFIC_SOURCE = "ncu capture, profiles/fused_qkv_exchange_c1shape.md"
+# NVLink user-data bytes sent by one launch of rank 0 of an SP group of two at
+# L=4096 (ncu nvltx__bytes_data_user.sum; profiles/fused_qkv_exchange_nvlink_sp2_L4096.md):
+# the algorithmic exchange volume 2*L*N*(S-1)/S plus two 32-byte flag writes.
+PROFILED_NVLINK_SP2 = {4096: 25165888}
 
 
 # ---------------------------------------------------------------- clocks
@@ -429,11 +437,101 @@ def workload_config(n, tokens):
     }
 
 
+# ---------------------------------------------------------------- NVLink capture
+def nvlink_capture(args):
+    """An SP group of two in one process: rank r runs on GPU r and stores its
+    peer's heads into the other GPU's receive buffers over NVLink.  Each
+    rank's kernel is launched with FU_FWD_NO_PEER_WAIT (the ranks never wait
+    for one another, so a profiler may serialise and replay one rank's launch
+    on its own); peer access is enabled both ways.  Checks the placement of
+    every received row against the oracle's exchange of the kernels' own
+    projections, and prints the event-timed launch of rank 0 with the
+    algorithmic NVLink bytes it sends."""
+    from cuda.bindings import runtime as rt
+
+    from flash_ulysses_b200 import _C
+    from oracle import ulysses_oracle as oracle
+
+    if torch.cuda.device_count() < 2:
+        raise SystemExit("--nvlink-capture needs two GPUs")
+    for d in (0, 1):
+        (err,) = rt.cudaSetDevice(d)
+        assert err == rt.cudaError_t.cudaSuccess, err
+        (err,) = rt.cudaDeviceEnablePeerAccess(1 - d, 0)
+        if err not in (rt.cudaError_t.cudaSuccess,
+                       rt.cudaError_t.cudaErrorPeerAccessAlreadyEnabled):
+            raise SystemExit(f"cudaDeviceEnablePeerAccess({d} -> {1 - d}): {err}")
+    S, L = 2, args.tokens
+    topo = oracle.Topology(S, S, Q_HEADS, KV_HEADS, HIDDEN)
+    widths = [w // S for w in topo.widths()]
+    devs = [torch.device("cuda", d) for d in (0, 1)]
+    recv = [tuple(torch.full((S * L, w), float("nan"), dtype=torch.bfloat16, device=dev)
+                  for w in widths) for dev in devs]
+    sync = [torch.zeros(_C.FU_SYNC_WORDS, dtype=torch.int32, device=dev) for dev in devs]
+    status = _C.StatusWord()
+    ops, inputs, projs = [], [], []
+    for r in (0, 1):
+        torch.cuda.set_device(r)
+        t = _C.Topology()
+        t.device, t.sp_size, t.sp_rank = r, S, r
+        t.q_heads, t.kv_heads, t.hidden_size, t.capacity_rows = Q_HEADS, KV_HEADS, HIDDEN, S * L
+        for d in (0, 1):
+            t.q_recv[d], t.k_recv[d], t.v_recv[d] = (b.data_ptr() for b in recv[d])
+            t.sync[d] = sync[d].data_ptr()
+        t.status, t.status_host = status.device_ptr, status.host_ptr
+        ops.append(_C.QkvOp(t))
+        inputs.append(make_inputs(S, r, L, seed=0))
+        projs.append(torch.empty(L, topo.packed_width, dtype=torch.bfloat16, device=devs[r]))
+    events = []
+    for i in range(args.warmup + args.steps):
+        for r in (0, 1):
+            torch.cuda.set_device(r)
+            x, pos, p = inputs[r]
+            if r == 0 and i >= args.warmup:
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record()
+            _C.launch(x, p["qkv_weight"], pos, p["q_norm_weight"], p["k_norm_weight"],
+                      p["rope_cache"], ops[r], q_epsilon=p["q_epsilon"], k_epsilon=p["k_epsilon"],
+                      flags=_C.FU_FWD_NO_PEER_WAIT, gemm_out=projs[r])
+            if r == 0 and i >= args.warmup:
+                end.record()
+                events.append((start, end))
+    for d in (0, 1):
+        torch.cuda.synchronize(d)
+    if status.value:
+        raise SystemExit("device status " + _C.decode_status(status.value))
+    # Every received row is where the oracle's exchange of these projections puts it.
+    cpu = []
+    for r in (0, 1):
+        x, pos, p = inputs[r]
+        cpu.append(({k: (v.cpu() if torch.is_tensor(v) else v) for k, v in p.items()}))
+    want = oracle.simulate_world(topo, [inputs[r][0].cpu() for r in (0, 1)],
+                                 [inputs[r][1].cpu() for r in (0, 1)], cpu,
+                                 projections=[projs[r].cpu() for r in (0, 1)])
+    exact = all(torch.equal(recv[d][c].cpu().view(torch.int16), want[d][c].view(torch.int16))
+                for d in (0, 1) for c in range(3))
+    ms = statistics.median(a.elapsed_time(b) for a, b in events)
+    nvl = 2 * L * topo.packed_width * (S - 1) // S
+    print(json.dumps({"mode": "nvlink-capture", "tokens_per_rank": L, "sp_size": S,
+                      "kernel_ms_rank0": round(ms, 5),
+                      "nvlink_bytes_per_launch_algorithmic": nvl,
+                      "algorithmic_gbs": round(nvl / (ms * 1e-3) / 1e9, 1),
+                      "outputs_bit_exact_vs_oracle_exchange": exact}), flush=True)
+    for op in ops:
+        op.destroy()
+    status.free()
+    if not exact:
+        raise SystemExit(1)
+
+
 # ---------------------------------------------------------------- our arm
 def main():
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
+        return
+    if args.nvlink_capture:
+        nvlink_capture(args)
         return
     world, rank, local = dist_env()
     n = max(world, 1)
@@ -514,6 +612,11 @@ def main():
         else:
             nvlink["measured"] = ("unavailable: NVML NVLink byte counters not readable "
                                   f"({nvl.errors if nvl is not None else 'no counter'})")[:400]
+        if tokens in PROFILED_NVLINK_SP2 and HIDDEN == 4096 and Q_HEADS == 32:
+            nvlink["profiled_sp2"] = {
+                "nvltx_user_bytes_per_launch": PROFILED_NVLINK_SP2[tokens],
+                "algorithmic_bytes_per_launch": 2 * tokens * ctx.packed_width // 2,
+                "source": "ncu capture, profiles/fused_qkv_exchange_nvlink_sp2_L4096.md"}
 
     # The reference harness's per-call method (rendezvous between calls).
     iso = time_isolated(step, min(args.steps, 20), n, group)
