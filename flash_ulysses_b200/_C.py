@@ -30,7 +30,6 @@ FU_FWD_SINGLE = 1 << 12
 FU_FWD_PAIR = 2 << 12
 FU_FWD_NO_RETILE = 1 << 14
 FU_FWD_FP32_EPILOGUE = 1 << 15
-FU_FWD_STREAMK = 1 << 16
 FU_FWD_NO_PDL = 1 << 17
 FU_OPROJ_READY = FU_SYNC_WORDS
 FU_OPROJ_GATHER_ONLY = 1 << 20

@@ -87,7 +87,7 @@ static_assert(NUM_BARS * 8 <= 256, "barrier area");
 static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KiB per-CTA shared memory limit");
 
 // Where a wait gave up (second byte of the status word).
-enum : int { W_EMPTY = 1, W_FULL = 2, W_TEMPTY = 3, W_TFULL = 4, W_DRAIN = 5, W_PARTIAL = 6 };
+enum : int { W_EMPTY = 1, W_FULL = 2, W_TEMPTY = 3, W_TFULL = 4, W_DRAIN = 5 };
 
 struct __align__(64) QkvParams {
     CUtensorMap tm_x;                       // X [L, H]: box {64, 128}
@@ -110,9 +110,6 @@ struct __align__(64) QkvParams {
     uint32_t fp32_epilogue;                 // 1: no BF16 rounding before the final store
     int32_t splits;                         // >1: split-K over a cluster of this many CTAs
     void* out_base[3 * FU_MAX_SP];          // receive buffers (split mode stores rows directly)
-    int32_t streamk;                        // pair grid: split the (tile, k-block) space evenly
-    float* ws;                              // stream-K partials: [pair][rank][256 cols][128 rows]
-    uint32_t* ws_flags;                     // [pair][rank][warp]: epoch of the partial in ws
     int32_t num_units;                      // work units of the persistent grid
     int32_t full_units;                     // units [0, full_units) are whole tiles; each later
                                             // pair of units is one tile's two heads
@@ -203,8 +200,10 @@ __device__ __forceinline__ Sched make_sched(const QkvParams& p) {
 }
 
 // A work unit of the persistent grid: a whole tile (both heads, half = -1),
-// or one head of a tile (half = 0 or 1).  The last, partial round of a pair
-// grid is re-tiled into one-head units so that it takes half as long.
+// or one head of a tile (half = 0 or 1).  A last, partial round of a pair grid
+// that at most half fills the pairs is re-tiled into one-head units, spread
+// over twice as many pairs (measured on B200, c1 shape: L=1024 53.5 us against
+// 57.2 us with whole tiles; neutral at L >= 4096).
 struct Unit {
     int m_blk, n_blk, half;
 };
@@ -225,51 +224,22 @@ __device__ __forceinline__ Unit decode_unit(const QkvParams& p, int u) {
     return un;
 }
 
-// One work item of a CTA: a unit over k-blocks [kb0, kb1) with a role.
-//   ROLE_EMIT   the item completes its unit (every mode but stream-K splits);
-//   ROLE_DUMP   stream-K: the head part of a tile, processed first by its pair
-//               (stream-K ranges are walked from their end); the FP32 partial
-//               goes to the workspace slot of this pair;
-//   ROLE_FOLD   stream-K: the tail part of the same tile, the last stream-K item
-//               of the next pair; the partial is added to its accumulator, then
-//               the tile is emitted.
-// The waiting pair always has the higher index, so no pair waits for one that
-// may not have been scheduled yet.
-enum : int { ROLE_EMIT = 0, ROLE_DUMP = 1, ROLE_FOLD = 2 };
+// One work item of a CTA: a unit over k-blocks [kb0, kb1).
 struct Item {
     Unit un;
-    int kb0, kb1, role, slot;
+    int kb0, kb1;
 };
 
-// Position of a CTA in its work list.  Stream-K (pair grid with P pairs and T
-// tiles, T >= P): tiles [0, sk_tiles) with sk_tiles = T - (T/P - 1) * P, one
-// to two rounds, are spread evenly over the pairs in the (tile, k-block)
-// space and walked first; the remaining full rounds follow data-parallel in
-// tile order (pair q takes tiles sk_tiles + q, + P, ...), so that the pairs
-// working at the same time share operand tiles in L2, and a fold's epilogue
-// overlaps the main loop of the next tile.
+// Position of a CTA in its work list: units first, first + stride, ...
 struct Walk {
-    int64_t cursor, limit;                  // stream-K position (moving down) and its end
-    int next, end, stride;                  // unit index, its end, its step
+    int next, end, stride;
 };
-
-__device__ __forceinline__ int streamk_tiles(const QkvParams& p, int pairs) {
-    return p.num_tiles - (p.num_tiles / pairs - 1) * pairs;
-}
 
 __device__ __forceinline__ Walk make_walk(const QkvParams& p, const Sched& sc) {
     Walk w;
     w.next = sc.first;
     w.end = sc.end;
     w.stride = sc.stride;
-    w.cursor = w.limit = 0;
-    if (p.streamk) {
-        const int sk_tiles = streamk_tiles(p, sc.stride);
-        const int64_t total = static_cast<int64_t>(sk_tiles) * p.k_blocks;
-        w.limit = total * sc.first / sc.stride;
-        w.cursor = total * (sc.first + 1) / sc.stride;
-        w.next = sk_tiles + sc.first;
-    }
     return w;
 }
 
@@ -277,34 +247,10 @@ __device__ __forceinline__ Walk make_walk(const QkvParams& p, const Sched& sc) {
 // more work.
 __device__ __forceinline__ bool next_item(const QkvParams& p, const Sched& sc, Walk& w,
                                           Item& it) {
-    if (p.streamk && w.cursor > w.limit) {
-        const int tile = static_cast<int>((w.cursor - 1) / p.k_blocks);
-        const int64_t tile_start = static_cast<int64_t>(tile) * p.k_blocks;
-        const int64_t lo = w.limit > tile_start ? w.limit : tile_start;
-        it.kb0 = static_cast<int>(lo - tile_start);
-        it.kb1 = static_cast<int>(w.cursor - tile_start);
-        it.un.m_blk = tile / p.num_n_blocks;
-        it.un.n_blk = tile % p.num_n_blocks;
-        it.un.half = -1;
-        if (it.kb1 < p.k_blocks) {
-            it.role = ROLE_DUMP;             // head part: the range ends inside this tile
-            it.slot = sc.first;
-        } else if (it.kb0 > 0) {
-            it.role = ROLE_FOLD;             // tail part: the range starts inside this tile
-            it.slot = sc.first - 1;
-        } else {
-            it.role = ROLE_EMIT;
-            it.slot = 0;
-        }
-        w.cursor = lo;
-        return true;
-    }
     if (w.next >= w.end) return false;
     it.un = decode_unit(p, w.next);
     it.kb0 = sc.kb0;
     it.kb1 = sc.kb1;
-    it.role = ROLE_EMIT;
-    it.slot = 0;
     w.next += w.stride;
     return true;
 }
@@ -759,63 +705,6 @@ __device__ void run_epilogue(const QkvParams& p, const Sched& sc, uint8_t* smem,
             break;
         tc_fence_after();
         const uint32_t acc_addr = tmem_base + lane_addr + acc * BN;
-        if (it.role != ROLE_EMIT) {
-            // Stream-K partial of this CTA's 128 rows: [256 cols][128 rows] FP32, so a
-            // warp's lanes touch consecutive rows of one column.
-            // Warp q of the folding CTA needs exactly the rows warp q of the dumping
-            // CTA wrote, so each warp has its own flag: [slot][rank][quarter].
-            float* part = p.ws + (static_cast<int64_t>(it.slot) * 2 + sc.rank) * (BN * BM);
-            uint32_t* flag = p.ws_flags + (it.slot * 2 + sc.rank) * 4 + quarter;
-            if (it.role == ROLE_DUMP) {
-#pragma unroll 1
-                for (int c = 0; c < BN; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld_32cols(acc_addr + c, r);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        __stcg(part + (c + i) * BM + row_in_tile, __uint_as_float(r[i]));
-                }
-                __syncwarp();
-                if (lane == 0) {
-                    __threadfence();
-                    st_release_gpu_u32(flag, epoch);
-                }
-                tc_fence_before();
-                if (kPair && sc.rank != 0)
-                    mbar_arrive_remote(map_cluster_smem(b.tempty + 8 * acc, 0));
-                else
-                    mbar_arrive(b.tempty + 8 * acc);
-                continue;
-            }
-            // ROLE_FOLD: wait (bounded) for the previous pair's partial, add it in TMEM.
-            if (lane == 0) {
-                const uint64_t t0 = globaltimer_ns();
-                while (ld_acquire_gpu_u32(flag) != epoch) {
-                    if (globaltimer_ns() - t0 > p.timeout_ns) {
-                        report_status(p.status, FU_DEV_PIPELINE_TIMEOUT, W_PARTIAL);
-                        *abort_flag = 1;
-                        break;
-                    }
-                }
-            }
-            __syncwarp();
-            // 32 columns per step: the partial's loads are issued before the
-            // accumulator's, so each step waits for one L2 round trip.
-#pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
-                float pv[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) pv[i] = __ldcg(part + (c + i) * BM + row_in_tile);
-                uint32_t r[32];
-                tmem_ld_32cols(acc_addr + c, r);
-                tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) + pv[i]);
-                tmem_st_32cols(acc_addr + c, r);
-            }
-            tmem_st_wait();
-        }
         // Heads of this unit: both of the tile (odd head count: the last tile
         // has one), or the single head of a one-head unit (accumulator column 0).
         const int h0 = n_blk * 2 + (un.half >= 0 ? un.half : 0);
@@ -1267,8 +1156,6 @@ struct fu_qkv_ctx {
     int sm_count = 0;
     int max_clusters[9] = {0};    // co-resident clusters of each size (index = CTAs per cluster)
     int max_pairs = 0;            // co-resident CTA pairs of the pair variant
-    float* ws = nullptr;          // stream-K partials, max_pairs + 1 slots
-    uint32_t* ws_flags = nullptr;
     uint32_t epoch = 0;
     int last_grid = 0;
     // Tensor-map caches: encoded maps of recently seen inputs (weights are
@@ -1394,19 +1281,6 @@ extern "C" int fu_qkv_create(const fu_qkv_topology* topo, fu_qkv_ctx** out) {
             ctx->max_pairs = n;
         }
     }
-    // Stream-K workspace: one slot of two 128 x 256 FP32 partials per pair.
-    if (ctx->max_pairs > 0) {
-        const size_t slots = static_cast<size_t>(ctx->max_pairs) + 1;
-        if (cudaMalloc(&ctx->ws, slots * 2 * BN * BM * sizeof(float)) != cudaSuccess ||
-            cudaMalloc(&ctx->ws_flags, slots * 2 * 4 * sizeof(uint32_t)) != cudaSuccess ||
-            cudaMemset(ctx->ws_flags, 0, slots * 2 * 4 * sizeof(uint32_t)) != cudaSuccess) {
-            cudaGetLastError();
-            cudaFree(ctx->ws);
-            cudaFree(ctx->ws_flags);
-            ctx->ws = nullptr;
-            ctx->ws_flags = nullptr;
-        }
-    }
     cudaSetDevice(prev);
     ctx->topo = *topo;
     if (ctx->topo.timeout_ns == 0) ctx->topo.timeout_ns = FU_DEFAULT_TIMEOUT_NS;
@@ -1417,14 +1291,6 @@ extern "C" int fu_qkv_create(const fu_qkv_topology* topo, fu_qkv_ctx** out) {
 }
 
 extern "C" int fu_qkv_destroy(fu_qkv_ctx* ctx) {
-    if (ctx != nullptr && (ctx->ws != nullptr || ctx->ws_flags != nullptr)) {
-        int prev = 0;
-        cudaGetDevice(&prev);
-        cudaSetDevice(ctx->topo.device);
-        cudaFree(ctx->ws);
-        cudaFree(ctx->ws_flags);
-        cudaSetDevice(prev);
-    }
     delete ctx;
     return FU_OK;
 }
@@ -1563,21 +1429,14 @@ extern "C" int fu_qkv_forward(fu_qkv_ctx* ctx, const void* x, const void* w,
     int grid;
     p.num_units = p.num_tiles;
     p.full_units = p.num_tiles;
-    p.streamk = 0;
-    p.ws = ctx->ws;
-    p.ws_flags = ctx->ws_flags;
     if (pair) {
-        // Whole tiles fill full rounds of the co-resident pairs.  On request, with
-        // at least one tile per pair and a partial last round, stream-K spreads
-        // the first rounds' (tile, k-block) space evenly; otherwise a partial last
+        // Whole tiles fill full rounds of the co-resident pairs; a partial last
         // round that at most half fills the pairs is re-tiled into one-head units.
         const int64_t T = (L + 2 * BM - 1) / (2 * BM) * p.num_n_blocks;
         const int64_t P = ctx->max_pairs;
         const int64_t rem = T % P;
         int64_t units = T, full = T;
-        if (T >= P && rem > 0 && ctx->ws != nullptr && (flags & FU_FWD_STREAMK) != 0) {
-            p.streamk = 1;
-        } else if (rem > 0 && 2 * rem <= P && (flags & FU_FWD_NO_RETILE) == 0) {
+        if (rem > 0 && 2 * rem <= P && (flags & FU_FWD_NO_RETILE) == 0) {
             full = T - rem;
             units = T + rem;
         }

@@ -107,14 +107,6 @@ enum fu_device_status {
  * (flash_ulysses_kernel_hopper.cu:129-152).  Default: the reference PyTorch
  * path's rounding points (BF16 projection, BF16 after the norm). */
 #define FU_FWD_FP32_EPILOGUE (1u << 15)
-/* Stream-K on the pair grid (needs at least one 256 x 256 tile per
- * co-resident pair and a partial last round): the first one to two rounds of
- * tiles are split evenly over the pairs in the (tile, k-block) space, a tile
- * shared by two pairs being completed through an FP32 partial-sum workspace,
- * and the remaining rounds run data-parallel.  Off by default: on B200 the
- * partial last round of the data-parallel grid runs faster per tile than a
- * full one, which leaves stream-K slower at every measured size. */
-#define FU_FWD_STREAMK (1u << 16)
 /* Launch without programmatic dependent launch.  By default the kernel is
  * launched with cudaLaunchAttributeProgrammaticStreamSerialization: its
  * prologue (barrier set-up, TMEM allocation) may run while the previous

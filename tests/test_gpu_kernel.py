@@ -213,23 +213,19 @@ def test_split_k_cluster_reduction(tokens, splits):
 
 @pytest.mark.parametrize("tokens,variant", [
     (1, "pair"), (65, "pair"), (128, "pair"), (129, "pair"), (256, "pair"), (300, "pair"),
-    (1024, "pair"), (1024, "single"), (300, "single"), (1024, "pair_whole"), (4096, "pair"),
-    (1024, "pair_streamk"), (2048, "pair_streamk"), (4096, "pair_streamk"),
-    (8192, "pair_streamk"),
+    (1024, "pair"), (1024, "single"), (300, "single"), (1024, "pair_whole"), (2048, "pair"),
+    (4096, "pair"), (8192, "pair"),
 ])
 def test_persistent_variants(tokens, variant):
     """Persistent grid with one CTA per 128x256 tile, and with CTA pairs
-    (tcgen05 cta_group::2, 256x256 tiles, each CTA holding half of W).  At
-    1024 to 8192 tokens the pair grid has more tiles than pairs and a partial
-    last round, so "pair_streamk" splits tiles over k-blocks between
-    neighbouring pairs (partials added in TMEM), alone at 1024 tokens and
-    followed by data-parallel rounds above."""
+    (tcgen05 cta_group::2, 256x256 tiles, each CTA holding half of W).  A last
+    round that at most half fills the pairs is re-tiled into one-head units
+    ("pair_whole" keeps whole tiles)."""
     base = CONFIGS["c1"]
     cfg = base.__class__("c1_p1", 1, 1, base.hidden_size, base.num_heads, base.num_kv_heads,
                          base.tokens, base.max_position)
     flag = {"pair": _C.FU_FWD_PAIR, "single": _C.FU_FWD_SINGLE,
-            "pair_whole": _C.FU_FWD_PAIR | _C.FU_FWD_NO_RETILE,
-            "pair_streamk": _C.FU_FWD_PAIR | _C.FU_FWD_STREAMK}[variant]
+            "pair_whole": _C.FU_FWD_PAIR | _C.FU_FWD_NO_RETILE}[variant]
     check_group(run_group(cfg, tokens, splits=1, variant=flag))
 
 
@@ -282,8 +278,8 @@ def exact_world(S, H, q_heads, kv_heads, tokens, seed=0):
     (2, 128, 2, 2, 1, 1, 0), (1, 64, 1, 1, 200, 1, 0), (2, 256, 4, 2, 65, 4, 0),
     (4, 512, 8, 4, 130, 3, 0), (1, 512, 4, 2, 1, 8, 0), (2, 256, 4, 2, 300, 1, 2 << 12),
     (1, 64, 1, 1, 200, 1, 2 << 12), (4, 512, 8, 4, 130, 1, 1 << 12),
-    (4, 512, 8, 4, 2600, 1, (2 << 12) | (1 << 16)), (1, 1024, 8, 4, 5000, 1, 1 << 16),
-    (2, 512, 8, 4, 9000, 1, 1 << 16),
+    (4, 512, 8, 4, 2600, 1, 2 << 12), (1, 1024, 8, 4, 5000, 1, 0),
+    (2, 512, 8, 4, 9000, 1, 0), (2, 256, 4, 2, 2000, 1, (2 << 12) | (1 << 14)),
 ])
 def test_bit_exact_on_exact_inputs(S, H, q, kv, tokens, splits, variant):
     """Placement, padding, norm, RoPE and clipping, bit for bit."""

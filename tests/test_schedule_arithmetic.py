@@ -50,52 +50,6 @@ def test_pair_grid_emits_every_head_of_every_tile_once(L, heads, pairs, retile):
     assert emitted == Counter({(m, h): 1 for m in range(m_blocks) for h in range(heads)})
 
 
-def streamk_items(T, kb, P, pair):
-    """make_walk + next_item with p.streamk: the items of one pair, in order,
-    as (tile, kb0, kb1, role); roles 0 emit, 1 dump, 2 fold."""
-    sk_tiles = T - (T // P - 1) * P               # streamk_tiles
-    total = sk_tiles * kb
-    limit, cursor = total * pair // P, total * (pair + 1) // P
-    items = []
-    while cursor > limit:
-        tile = (cursor - 1) // kb
-        start = tile * kb
-        lo = max(limit, start)
-        kb0, kb1 = lo - start, cursor - start
-        role = 1 if kb1 < kb else (2 if kb0 > 0 else 0)
-        items.append((tile, kb0, kb1, role))
-        cursor = lo
-    for t in range(sk_tiles + pair, T, P):       # data-parallel rounds after
-        items.append((t, 0, kb, 0))
-    return items
-
-
-@settings(max_examples=200, deadline=None)
-@given(st.integers(1, 80), st.integers(0, 300), st.integers(1, 128))
-def test_streamk_accumulates_every_kblock_once_and_folds_into_a_dump(P, extra, kb):
-    T = P + extra                                 # stream-K requires T >= P
-    seen = Counter()
-    dumps, folds = {}, {}
-    for pair in range(P):
-        for i, (tile, kb0, kb1, role) in enumerate(streamk_items(T, kb, P, pair)):
-            for k in range(kb0, kb1):
-                seen[(tile, k)] += 1
-            # No item both starts and ends inside a tile (it would need a chain).
-            assert not (kb0 > 0 and kb1 < kb)
-            if role == 1:
-                assert i == 0                     # a pair's dump is its first item
-                dumps[tile] = (pair, kb1)
-            elif role == 2:
-                folds[tile] = (pair, kb0)
-    assert seen == Counter({(t, k): 1 for t in range(T) for k in range(kb)})
-    # Every split tile has one dump and one fold by the next pair, which waits
-    # on the dumping pair's slot (pair - 1): the waiting pair has the higher index.
-    assert dumps.keys() == folds.keys()
-    for tile, (pd, cut) in dumps.items():
-        pf, start = folds[tile]
-        assert pf == pd + 1 and start == cut
-
-
 # ---------------------------------------------------------------- output side (fu_oproj.cu)
 def slice_rows_for(cpm, unit_bytes=32 * 1024):
     """fu_oproj_forward: push units of ~32 KiB, 8 to 128 rows."""
