@@ -88,7 +88,7 @@ NVLINK_GBS = 770.0      # measured peer copy per direction on this pool (900 nom
 # DRAM bytes (read + write) per launch of the fused kernel at the c1 shape,
 # world of one, from ncu captures (dram__bytes_read.sum + dram__bytes_write.sum;
 # profiles/fused_qkv_exchange_c1shape.md).  Keyed by tokens per rank.
-PROFILED_TRAFFIC = {4096: 186390016.0}
+PROFILED_TRAFFIC = {4096: 141881344.0}
 PROFILED_TRAFFIC_SOURCE = "ncu capture, profiles/fused_qkv_exchange_c1shape.md"
 # NVLink user-data bytes sent by one launch of rank 0 of an SP group of two at
 # L=4096 (ncu nvltx__bytes_data_user.sum; profiles/fused_qkv_exchange_nvlink_sp2_L4096.md):

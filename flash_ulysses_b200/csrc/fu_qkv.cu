@@ -105,6 +105,7 @@ struct __align__(64) QkvParams {
     int32_t heads, q_heads, kv_heads;
     int32_t sp_size, sp_rank, q_per_gpu, kv_per_gpu;
     int32_t num_n_blocks, num_tiles, k_blocks;
+    int32_t num_m_tiles;                    // row blocks of tiles (128 rows, or 256 for a pair)
     float q_eps, k_eps;
     uint32_t wait_peers;
     uint32_t fp32_epilogue;                 // 1: no BF16 rounding before the final store
@@ -199,6 +200,12 @@ __device__ __forceinline__ Sched make_sched(const QkvParams& p) {
     return s;
 }
 
+// Tiles are numbered column-major (t -> row block t mod num_m_tiles, column
+// block t / num_m_tiles), so the pairs running at the same time share W's
+// column blocks and re-read X, the smaller operand, from L2: W streams from
+// HBM once per call (row-major numbering re-read all of W every round, and
+// the outputs written in between evicted part of it).
+//
 // A work unit of the persistent grid: a whole tile (both heads, half = -1),
 // or one head of a tile (half = 0 or 1).  A last, partial round of a pair grid
 // that at most half fills the pairs is re-tiled into one-head units, spread
@@ -211,14 +218,14 @@ struct Unit {
 __device__ __forceinline__ Unit decode_unit(const QkvParams& p, int u) {
     Unit un;
     if (u < p.full_units) {
-        un.m_blk = u / p.num_n_blocks;
-        un.n_blk = u % p.num_n_blocks;
+        un.m_blk = u % p.num_m_tiles;
+        un.n_blk = u / p.num_m_tiles;
         un.half = -1;
     } else {
         const int j = u - p.full_units;
         const int t = p.full_units + (j >> 1);
-        un.m_blk = t / p.num_n_blocks;
-        un.n_blk = t % p.num_n_blocks;
+        un.m_blk = t % p.num_m_tiles;
+        un.n_blk = t / p.num_m_tiles;
         un.half = j & 1;
     }
     return un;
@@ -736,7 +743,7 @@ __device__ void run_split_partial(const QkvParams& p, const Sched& sc, uint8_t* 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int quarter = warp & 3;
-    const int m_blk = sc.first / p.num_n_blocks;
+    const int m_blk = decode_unit(p, sc.first).m_blk;
     // Read now, used by the reduction's entry barrier (after the main loop).
     if (threadIdx.x == 64) *reinterpret_cast<volatile int32_t*>(smem + OFF_MISC + 12) =
         status_at_start(p);
@@ -754,7 +761,7 @@ __device__ void run_split_partial(const QkvParams& p, const Sched& sc, uint8_t* 
                 report_status(p.status, FU_DEV_POSITION_RANGE, 0);
             else
                 rope_row = static_cast<int32_t>(pos);
-            const int n_blk = sc.first % p.num_n_blocks;
+            const int n_blk = decode_unit(p, sc.first).n_blk;
             if (n_blk * 2 < p.q_heads + p.kv_heads) {          // a Q/K head in this tile
                 const float* r = p.rope + static_cast<int64_t>(rope_row) * 128;
 #pragma unroll
@@ -914,8 +921,9 @@ __device__ void run_split_reduce(const QkvParams& p, const Sched& sc, uint8_t* s
     if (!wait_peers_entered(p, epoch, abort_flag, false, status_seen)) return;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int m_blk = sc.first / p.num_n_blocks;
-    const int n_blk = sc.first % p.num_n_blocks;
+    const Unit tile = decode_unit(p, sc.first);
+    const int m_blk = tile.m_blk;
+    const int n_blk = tile.n_blk;
     const int rows = min(BM, p.L - m_blk * BM);
     const int heads_here = min(2, p.heads - n_blk * 2);
     const int items = rows * heads_here;
@@ -1410,6 +1418,7 @@ extern "C" int fu_qkv_forward(fu_qkv_ctx* ctx, const void* x, const void* w,
     p.num_n_blocks = (heads + 1) / 2;
     const int64_t m_blocks = (L + BM - 1) / BM;
     const int64_t tiles = m_blocks * p.num_n_blocks;
+    p.num_m_tiles = static_cast<int32_t>(m_blocks);
     if (tiles > INT32_MAX) return set_error(FU_ERR_INVALID, "too many tiles");
     p.num_tiles = static_cast<int32_t>(tiles);
     p.k_blocks = static_cast<int32_t>(H / BK);
@@ -1441,6 +1450,7 @@ extern "C" int fu_qkv_forward(fu_qkv_ctx* ctx, const void* x, const void* w,
             units = T + rem;
         }
         p.num_tiles = static_cast<int32_t>(T);
+        p.num_m_tiles = static_cast<int32_t>(T / p.num_n_blocks);
         p.num_units = static_cast<int32_t>(units);
         p.full_units = static_cast<int32_t>(full);
         grid = 2 * static_cast<int>(units < P ? units : P);
@@ -1647,6 +1657,7 @@ extern "C" int fu_qkv_forward_noalloc(int device, const void* x, const void* w,
     p.num_n_blocks = (heads + 1) / 2;
     const int64_t tiles = (L + BM - 1) / BM * p.num_n_blocks;
     p.num_tiles = static_cast<int32_t>(tiles);
+    p.num_m_tiles = static_cast<int32_t>((L + BM - 1) / BM);
     p.num_units = p.num_tiles;
     p.full_units = p.num_tiles;
     p.k_blocks = static_cast<int32_t>(hidden_size / BK);

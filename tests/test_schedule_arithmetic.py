@@ -26,13 +26,14 @@ def pair_grid(L, heads, pairs, retile=True):
     return T, units, full, min(units, pairs), nb
 
 
-def decode_unit(u, full_units, nb):
-    """fu_qkv.cu::decode_unit: (m_blk, n_blk, half); half -1 = both heads."""
+def decode_unit(u, full_units, nb, m_tiles):
+    """fu_qkv.cu::decode_unit: (m_blk, n_blk, half); half -1 = both heads.
+    Tiles are numbered column-major (row block t mod m_tiles)."""
     if u < full_units:
-        return u // nb, u % nb, -1
+        return u % m_tiles, u // m_tiles, -1
     j = u - full_units
     t = full_units + (j >> 1)
-    return t // nb, t % nb, j & 1
+    return t % m_tiles, t // m_tiles, j & 1
 
 
 @settings(max_examples=200, deadline=None)
@@ -42,7 +43,7 @@ def test_pair_grid_emits_every_head_of_every_tile_once(L, heads, pairs, retile):
     emitted = Counter()
     for pair in range(grid):                       # make_sched<true>: first, stride
         for u in range(pair, units, grid):
-            m, n, half = decode_unit(u, full, nb)
+            m, n, half = decode_unit(u, full, nb, T // nb)
             for h in ((0, 1) if half < 0 else (half,)):
                 if 2 * n + h < heads:              # an odd head count leaves one slot empty
                     emitted[(m, 2 * n + h)] += 1
