@@ -98,6 +98,8 @@ struct OprojParams {
     unsigned long long timeout_ns;
     int32_t L, H, K, cpm, sp_size, sp_rank;
     int32_t num_m, num_n, num_tiles, k_blocks, units;
+    int32_t row_tiles;                        // tile rows (128 rows, or 256 for a pair)
+    int32_t col_major;                        // 1: tiles numbered column-major (see Sched)
     int32_t bn;                        // output columns per tile: 256, 128 or 64
     int32_t stages, stage_bytes;       // operand ring: RING_BYTES / stage_bytes stages
     int32_t slice_rows, slices;        // push unit: slice_rows rows; slices = BM / slice_rows
@@ -242,10 +244,17 @@ struct Sched {
         first = kPair ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
         stride = kPair ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
     }
-    // This CTA's 128-row m-block of tile t.
+    // This CTA's 128-row m-block of tile t, and the tile's column block.
+    // With peers pushing rows in (S > 1) tiles go row by row, so the first
+    // rounds need only the m-blocks that complete first; with nothing to wait
+    // for (S = 1) they go column by column, so the CTAs running at the same
+    // time share W_o's column blocks and W_o streams from HBM once.
     __device__ int m_block(const OprojParams& p, int t) const {
-        const int mt = t / p.num_n;
+        const int mt = p.col_major ? t % p.row_tiles : t / p.num_n;
         return kPair ? 2 * mt + rank : mt;
+    }
+    __device__ int n_block(const OprojParams& p, int t) const {
+        return p.col_major ? t / p.row_tiles : t % p.num_n;
     }
 };
 
@@ -268,7 +277,7 @@ __device__ void run_producer(const OprojParams& p, uint8_t* smem, const Bars& b,
     bool ok = true;
     for (int t = sc.first; ok && t < p.num_tiles; t += sc.stride) {
         const int mb = sc.m_block(p, t);
-        const int nb = t % p.num_n;
+        const int nb = sc.n_block(p, t);
         if (mb > ready_m && target > 0 && mb < p.num_m) {
             // Every source's slices of this m-block have landed in G.
             const uint64_t t0 = globaltimer_ns();
@@ -426,7 +435,7 @@ __device__ void run_epilogue(const OprojParams& p, uint8_t* smem, uint32_t tmem_
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         const int mb = sc.m_block(p, t);
-        const int nb = t % p.num_n;
+        const int nb = sc.n_block(p, t);
         if (!fu_wait_parity(b.tfull + 8 * acc, acc_phase, abort_flag, p.timeout_ns, p.status,
                             W_TFULL))
             break;
@@ -787,6 +796,8 @@ extern "C" int fu_oproj_forward(fu_oproj_ctx* ctx, const void* attn, const void*
     p.stages = oproj::RING_BYTES / p.stage_bytes;
     if (p.stages > oproj::MAX_STAGES) p.stages = oproj::MAX_STAGES;
     p.num_n = static_cast<int32_t>(H / bn);
+    p.row_tiles = static_cast<int32_t>(row_tiles);
+    p.col_major = S == 1 ? 1 : 0;
     p.num_tiles = do_gemm ? static_cast<int32_t>(row_tiles) * p.num_n : 0;
     p.k_blocks = static_cast<int32_t>(K / oproj::BK);
     // Push units of ~32 KiB: 8 to 128 rows (a power of two) of cpm columns.

@@ -113,10 +113,11 @@ def test_push_unit_sizes():
 
 @settings(max_examples=150, deadline=None)
 @given(st.integers(1, 9000), st.sampled_from([256, 512, 1024, 2048, 4096, 8192]),
-       st.integers(1, 74), st.booleans())
-def test_oproj_tiles_cover_the_output_once(L, H, pairs, pair):
-    """fu_oproj_forward's tiling and Sched<kPair>::m_block: every (row block,
-    column block) of out [L, H] is stored by exactly one CTA."""
+       st.integers(1, 74), st.booleans(), st.booleans())
+def test_oproj_tiles_cover_the_output_once(L, H, pairs, pair, col_major):
+    """fu_oproj_forward's tiling and Sched<kPair>::m_block / n_block (tiles
+    numbered row by row with peers, column by column for a world of one):
+    every (row block, column block) of out [L, H] is stored by exactly one CTA."""
     num_m = (L + BM - 1) // BM
     row_tiles = (L + 2 * BM - 1) // (2 * BM) if pair else num_m
     slots = pairs if pair else 148
@@ -133,7 +134,7 @@ def test_oproj_tiles_cover_the_output_once(L, H, pairs, pair):
         rank = cta % 2 if pair else 0
         first, stride = (cta // 2, ctas // 2) if pair else (cta, ctas)
         for t in range(first, tiles, stride):
-            mt, nb = divmod(t, num_n)
+            mt, nb = (t % row_tiles, t // row_tiles) if col_major else divmod(t, num_n)
             mb = 2 * mt + rank if pair else mt
             if mb < num_m:                        # a pair's second CTA may have no rows
                 stored[(mb, nb)] += 1
