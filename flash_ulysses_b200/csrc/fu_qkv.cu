@@ -1093,14 +1093,25 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
         cluster_sync_all();                 // peers are done reading this CTA's partial
     }
 
-    // Every CTA's output is complete (stores waited for, then the barriers
-    // above).  A world of one needs only GPU scope; with peers, one
-    // system-scope fence per CTA makes its remote stores visible beyond this
-    // GPU before it is counted, and the last CTA's release stores publish the
-    // epoch (cumulative over every counted CTA).
+    // A world of one: no peer reads the exit flag, and the next call reads the
+    // epoch only once this grid has completed, so CTA 0 alone advances it when
+    // it is done (every CTA read this call's epoch at its start; one that
+    // starts later -- a second wave of split clusters -- uses the epoch for
+    // nothing) and no CTA counts in.
+    if (p.sp_size == 1) {
+        if (blockIdx.x == 0 && threadIdx.x == 64) {
+            *reinterpret_cast<volatile uint32_t*>(my_sync + FU_SYNC_EPOCH) = epoch;
+            *reinterpret_cast<volatile uint32_t*>(my_sync) = epoch;
+        }
+        return;
+    }
+    // With peers: every CTA's output is complete (stores waited for, then the
+    // barriers above); one system-scope fence per CTA makes its remote stores
+    // visible beyond this GPU before it is counted, and the last CTA publishes
+    // the epoch (cumulative over every counted CTA).
     if (threadIdx.x == 64) {
         const bool aborted = *abort_flag != 0;
-        if (p.sp_size > 1) fence_acq_rel_sys(); else fence_acq_rel_gpu();
+        fence_acq_rel_sys();
         const uint32_t old =
             atom_add_acq_rel_gpu_u32(my_sync + FU_SYNC_COUNTER, aborted ? 0x10001u : 1u);
         if ((old & 0xFFFFu) == gridDim.x - 1) {
@@ -1111,27 +1122,22 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
             *reinterpret_cast<volatile uint32_t*>(my_sync + FU_SYNC_EPOCH) = epoch;
             // A failed call of a group marks the operator failed: calls queued
             // behind it skip their peer waits and stores.
-            if (any_abort && p.sp_size > 1)
+            if (any_abort)
                 *reinterpret_cast<volatile uint32_t*>(my_sync + FU_SYNC_FAILED) = 1u;
             if (!any_abort) {
-                if (p.sp_size == 1) {
-                    st_release_gpu_u32(my_sync, epoch);
-                } else {
-                    // One system-scope fence orders every counted CTA's stores
-                    // (acquired through the counter) before all the flags; the
-                    // flags themselves are posted stores.
-                    fence_acq_rel_sys();
-                    for (int d = 0; d < p.sp_size; ++d)
-                        st_relaxed_sys_u32(p.sync[d] + p.sp_rank, epoch);
-                    if (p.wait_peers) {
-                        const uint64_t t0 = globaltimer_ns();
-                        for (int s = 0; s < p.sp_size; ++s) {
-                            while (static_cast<int32_t>(ld_acquire_sys_u32(my_sync + s) - epoch) <
-                                   0) {
-                                if (globaltimer_ns() - t0 > p.timeout_ns) {
-                                    report_status(p.status, FU_DEV_PEER_TIMEOUT, s);
-                                    break;
-                                }
+                // One system-scope fence orders every counted CTA's stores
+                // (acquired through the counter) before all the flags; the
+                // flags themselves are posted stores.
+                fence_acq_rel_sys();
+                for (int d = 0; d < p.sp_size; ++d)
+                    st_relaxed_sys_u32(p.sync[d] + p.sp_rank, epoch);
+                if (p.wait_peers) {
+                    const uint64_t t0 = globaltimer_ns();
+                    for (int s = 0; s < p.sp_size; ++s) {
+                        while (static_cast<int32_t>(ld_acquire_sys_u32(my_sync + s) - epoch) < 0) {
+                            if (globaltimer_ns() - t0 > p.timeout_ns) {
+                                report_status(p.status, FU_DEV_PEER_TIMEOUT, s);
+                                break;
                             }
                         }
                     }
