@@ -453,6 +453,27 @@ __device__ __forceinline__ void cluster_sync_all() {
                  "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// The two halves of cluster_sync_all, for an early arrive and a late wait.
+// The relaxed arrive orders no memory (an mbarrier initialisation is published
+// by fence.mbarrier_init.release.cluster before it).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Bulk copy of `bytes` (a multiple of 16, 16-byte aligned) from this CTA's
+// shared memory to another cluster CTA's (`dst_cluster`), completion counted
+// on that CTA's mbarrier `bar_cluster`.
+__device__ __forceinline__ void bulk_copy_s2cluster(uint32_t dst_cluster, uint32_t src,
+                                                    uint32_t bytes, uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(dst_cluster), "r"(src), "r"(bytes), "r"(bar_cluster) : "memory");
+}
+
 // Address of `local_smem_addr` in the shared memory of cluster CTA `rank`.
 __device__ __forceinline__ uint32_t map_cluster_smem(uint32_t local_smem_addr, uint32_t rank) {
     uint32_t r;

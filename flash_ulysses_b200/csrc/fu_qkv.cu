@@ -74,7 +74,7 @@ constexpr int OFF_A = 0;
 constexpr int OFF_STG = Ring<false>::BYTES;
 constexpr int OFF_BAR = OFF_STG + 4 * STAGING_PER_WARP;
 constexpr int MAX_STAGES = 6;
-constexpr int NUM_BARS = 2 * MAX_STAGES + 2 + 2 + 1;
+constexpr int NUM_BARS = 2 * MAX_STAGES + 2 + 2 + 1 + 1;
 constexpr int OFF_MISC = OFF_BAR + 256;
 constexpr int OFF_GAMMA = OFF_MISC + 64;
 constexpr int SMEM_BYTES = OFF_GAMMA + 2 * 128 * 4;
@@ -110,6 +110,7 @@ struct __align__(64) QkvParams {
     uint32_t wait_peers;
     uint32_t fp32_epilogue;                 // 1: no BF16 rounding before the final store
     int32_t splits;                         // >1: split-K over a cluster of this many CTAs
+    int32_t split_push;                     // split mode, few rows: partials pushed to the leader
     void* out_base[3 * FU_MAX_SP];          // receive buffers (split mode stores rows directly)
     int32_t num_units;                      // work units of the persistent grid
     int32_t full_units;                     // units [0, full_units) are whole tiles; each later
@@ -264,11 +265,26 @@ __device__ __forceinline__ bool next_item(const QkvParams& p, const Sched& sc, W
 
 // Shared-memory barrier layout (fixed offsets, up to MAX_STAGES stages).
 struct Bars {
-    uint32_t full, empty, tfull, tempty, mma_done;
+    uint32_t full, empty, tfull, tempty, mma_done, push;
     __device__ Bars(uint32_t base)
         : full(base), empty(base + 8 * MAX_STAGES), tfull(base + 16 * MAX_STAGES),
-          tempty(base + 16 * MAX_STAGES + 16), mma_done(base + 16 * MAX_STAGES + 32) {}
+          tempty(base + 16 * MAX_STAGES + 16), mma_done(base + 16 * MAX_STAGES + 32),
+          push(base + 16 * MAX_STAGES + 40) {}
 };
+
+// Split push mode: the staging area holds the tile's RoPE row indices
+// (512 bytes), then one 1 KiB FP32 row (256 columns) per valid token row and
+// cluster rank, [rank][row]: every CTA parks its rows in its own rank's slot,
+// and the leader (rank 0) receives the others' slots at the same offsets.
+constexpr int OFF_PUSH = OFF_STG + 512;
+constexpr int PUSH_ROW_BYTES = BN * 4;
+constexpr int PUSH_BYTES = 4 * STAGING_PER_WARP - 512;
+// After the [rank][row] slots: the valid rows' cos|sin (512 bytes each),
+// fetched by the leader while the tensor cores run.
+constexpr int ROPE_ROW_BYTES = 128 * 4;
+__device__ __forceinline__ int push_rope_offset(const QkvParams& p) {
+    return OFF_PUSH + p.splits * p.L * PUSH_ROW_BYTES;
+}
 
 // Whether an earlier call of this operator gave up a wait: the sticky
 // FU_SYNC_FAILED word of this rank's own sync block, in device memory (a read
@@ -770,10 +786,43 @@ __device__ void run_split_partial(const QkvParams& p, const Sched& sc, uint8_t* 
         }
         reinterpret_cast<int32_t*>(smem + OFF_STG)[row] = rope_row;
     }
+    if (p.split_push && cluster_ctarank() == 0) {
+        // The leader reduces every item: bring the valid rows' cos|sin into
+        // shared memory now, 16 bytes per thread per step.
+        named_bar_sync(1, NUM_EPI_THREADS);          // the row indices above
+        const int32_t* rows_idx = reinterpret_cast<const int32_t*>(smem + OFF_STG);
+        const uint32_t dst = smem_u32(smem + push_rope_offset(p));
+        for (int i = threadIdx.x - 64; i < p.L * 32; i += NUM_EPI_THREADS) {
+            const int r = i >> 5, c = i & 31;
+            cp_async_16(dst + r * ROPE_ROW_BYTES + c * 16,
+                        p.rope + static_cast<int64_t>(rows_idx[r]) * 128 + c * 4);
+        }
+        cp_async_wait_all();
+    }
     if (!fu_wait_parity(b.tfull, 0, abort_flag, p.timeout_ns, p.status, W_TFULL)) return;
     tc_fence_after();
     if (m_blk * BM + quarter * 32 >= p.L) return;          // no valid row in this warp
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    if (p.split_push) {
+        // Push mode (a single block of at most a few rows): this rank's slot.
+        const int r = quarter * 32 + lane;
+        float* slot = reinterpret_cast<float*>(
+            smem + OFF_PUSH + (static_cast<int>(cluster_ctarank()) * p.L + r) * PUSH_ROW_BYTES);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld_32cols(tmem_base + lane_addr + c * 32, v);
+            tmem_ld_wait();
+            if (r < p.L)
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    reinterpret_cast<float4*>(slot + c * 32)[i] =
+                        make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                    __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+        }
+        fence_proxy_async_smem();          // read next by a bulk copy (async proxy)
+        return;
+    }
     float* row = reinterpret_cast<float*>(smem + OFF_A + (quarter * 32 + lane) * PART_STRIDE);
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
@@ -986,6 +1035,44 @@ __device__ void run_split_reduce(const QkvParams& p, const Sched& sc, uint8_t* s
     }
 }
 
+// Split push mode, the leader's epilogue warps: every rank's rows of the
+// single row block are in this CTA's shared memory, [rank][row][256 cols].
+// One item = one valid token row x one head, one warp per item, lane l owning
+// columns 4l..4l+3; partials summed in rank order (deterministic), then the
+// same normalisation, rotation and store as the distributed reduction.
+__device__ void run_split_push_reduce(const QkvParams& p, const Sched& sc, uint8_t* smem,
+                                      const float* gam, volatile int* abort_flag,
+                                      uint32_t epoch) {
+    const int32_t status_seen = *reinterpret_cast<volatile int32_t*>(smem + OFF_MISC + 12);
+    if (!wait_peers_entered(p, epoch, abort_flag, false, status_seen)) return;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const Unit tile = decode_unit(p, sc.first);
+    const int rows = p.L;
+    const int heads_here = min(2, p.heads - tile.n_blk * 2);
+    const int items = rows * heads_here;
+    const float* rope_smem = reinterpret_cast<const float*>(smem + push_rope_offset(p));
+    const float* slots = reinterpret_cast<const float*>(smem + OFF_PUSH);
+    for (int i = warp - 2; i < items; i += NUM_EPI_THREADS / 32) {
+        const int r = i / heads_here, hs = i % heads_here;
+        const int h = tile.n_blk * 2 + hs;
+        SplitRope rope;
+        rope.cs = rope.sn = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (h < p.q_heads + p.kv_heads) {
+            const float* cs = rope_smem + r * 128 + 4 * (lane & 15);
+            rope.cs = *reinterpret_cast<const float4*>(cs);
+            rope.sn = *reinterpret_cast<const float4*>(cs + 64);
+        }
+        float4 acc = reinterpret_cast<const float4*>(slots + r * BN + hs * 128)[lane];
+        for (int k = 1; k < p.splits; ++k) {
+            const float4 v =
+                reinterpret_cast<const float4*>(slots + (k * rows + r) * BN + hs * 128)[lane];
+            acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+        }
+        split_item_emit(p, acc, r, h, gam, lane, rope);
+    }
+}
+
 // ------------------------------------------------------------ kernel
 template <bool kPair>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -1018,6 +1105,12 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
             mbar_init(b.tempty + 8 * a, kPair ? 2 * NUM_EPI_THREADS : NUM_EPI_THREADS);
         }
         mbar_init(b.mma_done, 1);
+        if (p.split_push && cluster_ctarank() == 0) {
+            mbar_init(b.push, 1);
+            // Every other rank's rows arrive by bulk copy.
+            const int rows = p.L;
+            mbar_arrive_expect_tx(b.push, static_cast<uint32_t>((p.splits - 1) * rows * PUSH_ROW_BYTES));
+        }
         *abort_flag = 0;
         fence_mbar_init();
         tma_prefetch_desc(&p.tm_x);
@@ -1050,6 +1143,9 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
     __syncthreads();
     // A pair's barriers and TMEM must exist in both CTAs before either uses them.
     if (kPair) cluster_sync_all();
+    // Split push mode: the leader's push barrier exists before any rank copies
+    // into it (this arrive, and the wait after the main loop).
+    if (split_mode && p.split_push) cluster_arrive_relaxed();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
     const uint32_t epoch = *epoch_slot;
@@ -1085,7 +1181,45 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
             tmem_dealloc(tmem_base, TMEM_COLS);
     }
 
-    if (split_mode) {
+    if (split_mode && p.split_push) {
+        // Every thread of every cluster CTA reaches both barriers on every path.
+        cluster_wait();                     // the leader's push barrier exists
+        const bool leader = cluster_ctarank() == 0;
+        if (!leader && threadIdx.x == 64) {
+            // This rank's rows (parked even after a failed wait, so the leader's
+            // barrier completes; the leader checks the abort flags) to the leader.
+            const uint32_t off = OFF_PUSH + cluster_ctarank() * p.L * PUSH_ROW_BYTES;
+            bulk_copy_s2cluster(map_cluster_smem(smem_u32(smem + off), 0), smem_u32(smem + off),
+                                static_cast<uint32_t>(p.L * PUSH_ROW_BYTES),
+                                map_cluster_smem(b.push, 0));
+        }
+        if (leader && warp >= 2) {
+            if (!drain_wait(b.push, 0, p.timeout_ns, p.status)) *abort_flag = 1;
+            // A rank that gave up has pushed an incomplete partial: store nothing.
+            // Its abort flag is read over distributed shared memory, so this must
+            // come before the leader's arrive below: the other ranks may exit as
+            // soon as every thread of the leader has arrived.
+            if (threadIdx.x == 64) {
+                const uint32_t flag_addr = smem_u32(const_cast<int*>(abort_flag));
+                uint32_t flags[FU_MAX_SP];
+#pragma unroll
+                for (int r = 0; r < FU_MAX_SP; ++r)
+                    flags[r] = r < p.splits ? ld_cluster_u32(map_cluster_smem(flag_addr, r)) : 0u;
+                uint32_t any = 0;
+#pragma unroll
+                for (int r = 0; r < FU_MAX_SP; ++r) any |= flags[r];
+                if (any) *abort_flag = 1;
+            }
+        }
+        // The leader: every copy has landed (its mbarrier saw the bytes) and no
+        // other rank's shared memory is read any more, so the others may exit.
+        cluster_arrive_relaxed();
+        if (leader && warp >= 2) {
+            named_bar_sync(1, NUM_EPI_THREADS);
+            if (*abort_flag == 0) run_split_push_reduce(p, sc, smem, gam, abort_flag, epoch);
+        }
+        cluster_wait();                     // the others keep their slots until then
+    } else if (split_mode) {
         // Every CTA of the cluster reaches both barriers on every path, so a
         // CTA that gave up on a wait cannot strand its peers here.
         cluster_sync_all();                 // partials visible cluster-wide
@@ -1436,6 +1570,11 @@ extern "C" int fu_qkv_forward(fu_qkv_ctx* ctx, const void* x, const void* w,
 
     p.splits = choose_splits(ctx, tiles, p.k_blocks, L < BM ? L : BM,
                              static_cast<int>((flags >> 8) & 0xFu));
+    // A single row block of a few rows: the cluster's partials go to its leader
+    // (every rank's rows fit the leader's staging area).
+    p.split_push = p.splits > 1 && m_blocks == 1 &&
+                   (static_cast<int64_t>(p.splits) * PUSH_ROW_BYTES + ROPE_ROW_BYTES) * L <=
+                       PUSH_BYTES ? 1 : 0;
     // CTA pairs (256-row tiles) for the persistent grid once a call spans two
     // row blocks, unless the flags pin the variant.
     const uint32_t variant = (flags >> 12) & 0x3u;
