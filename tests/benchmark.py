@@ -32,6 +32,19 @@ projection round ~2e-3 of its BF16 outputs differently, and NeoX rotation
 turns a rare such flip into a violation of a tight tolerance (the CUDA
 kernels' own reduction order can do the same, far more rarely).
 
+``--baseline sglang`` adds the reference's second comparison
+(tests/sglang_base.py:16-80 in the reference): the serving framework's
+operator sequence -- ``F.linear`` with the ``[N, H]`` weight, per-head Q/K
+RMSNorm and NeoX RoPE from the cos|sin cache in place on the projection's
+Q/K views, BF16 norm weights, then the same pack + NCCL ``all_to_all_single``.
+sglang is not installed here, so the norm and rotation run as vLLM's
+precompiled ``fused_qk_norm_rope`` CUDA operator (one kernel over the packed
+projection) in place of sglang's ``fused_inplace_qknorm`` followed by its
+``apply_rope_with_cos_sin_cache_inplace``.  Its elements outside
+``--atol/--rtol`` are reported, not asserted: its rounding points (BF16 norm
+weights, FP32 from the norm through the rotation) are not the reference
+PyTorch path's.
+
 ``--o-proj`` (no counterpart in the reference) also runs the output side on
 each case's Q as the attention output: zero violations against an NCCL
 all_to_all of the source blocks followed by the FP32-accumulated projection,
@@ -49,7 +62,10 @@ sys.path.insert(0, os.path.dirname(HERE))
 
 def parse_args():
     p = argparse.ArgumentParser(description="GPU QKV correctness and latency comparisons")
-    p.add_argument("--baseline", nargs="+", choices=("torch",), default=["torch"])
+    p.add_argument("--baseline", nargs="+", choices=("torch", "sglang"), default=["torch"],
+                   help="torch: the reference's PyTorch path; sglang: the serving "
+                        "framework's operator sequence (vLLM's fused Q/K norm + RoPE "
+                        "operator standing in for sglang's, which is not installed)")
     p.add_argument("--sp-size", type=int, default=2)
     p.add_argument("--hidden-size", type=int, default=4096)
     p.add_argument("--q-heads", type=int, default=32)
@@ -123,6 +139,48 @@ def main(args):
         return oracle.unpack(topo, received, x.size(0))
 
     cpu_params = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in params.items()}
+
+    serving = None
+    vllm_ops = None
+    if "sglang" in args.baseline:
+        try:
+            from vllm import _custom_ops as vllm_ops
+            if not hasattr(torch.ops._C, "fused_qk_norm_rope"):
+                raise ImportError("vllm's CUDA operators did not load")
+        except Exception as e:              # reported; the other comparisons still run
+            say(f"serving-operator baseline unavailable: {type(e).__name__}: {e}"[:300])
+            vllm_ops = None
+    if vllm_ops is not None:
+        weight_nk = weight.t().contiguous()             # nn.Linear layout, prepared untimed
+        q_norm_bf16, k_norm_bf16 = q_norm, k_norm       # BF16, as the serving model keeps them
+        widths = topo.widths()
+        # The operator takes the cos|sin cache in FP32 or in the activations'
+        # dtype depending on its build; probe once, untimed.
+        serving_cache = params["rope_cache"]
+        try:
+            probe = torch.zeros(1, ctx.packed_width, device="cuda", dtype=torch.bfloat16)
+            vllm_ops.fused_qk_norm_rope(probe, topo.local_q_heads, topo.local_kv_heads,
+                                        topo.local_kv_heads, 128, params["q_epsilon"],
+                                        q_norm_bf16, k_norm_bf16, serving_cache, True,
+                                        torch.zeros(1, device="cuda", dtype=torch.int64))
+            torch.cuda.synchronize()
+        except RuntimeError:
+            serving_cache = params["rope_cache"].bfloat16()
+
+        def serving(x, positions):
+            """The reference's SGLang comparison (tests/sglang_base.py:44-80 in
+            the reference) with vLLM's fused norm + RoPE operator."""
+            qkv = torch.nn.functional.linear(x, weight_nk)
+            vllm_ops.fused_qk_norm_rope(qkv, topo.local_q_heads, topo.local_kv_heads,
+                                        topo.local_kv_heads, 128, params["q_epsilon"],
+                                        q_norm_bf16, k_norm_bf16, serving_cache, True,
+                                        positions)
+            q, k, v = qkv.split(widths, dim=-1)
+            parts = [t.reshape(x.size(0), S, -1) for t in (q, k, v)]
+            send = torch.cat(parts, dim=-1).transpose(0, 1).contiguous()
+            received = torch.empty_like(send)
+            dist.all_to_all_single(received, send, group=sp_group)
+            return oracle.unpack(topo, received, x.size(0))
 
     def oracle_on_projection(x, positions, projection):
         """The CPU oracle's epilogue on this rank's projection, then NCCL."""
@@ -225,6 +283,13 @@ def main(args):
         dist.all_reduce(untouched, op=dist.ReduceOp.MIN)
         ok &= bool(untouched.item())
         say(f"  correctness: {'PASS' if ok else 'FAIL'} (all Q/K/V rows and output boundary)")
+        if serving is not None:
+            served = serving(x, positions)
+            for c, name in enumerate("QKV"):
+                bad = (~torch.isclose(got[c], served[c], atol=args.atol, rtol=args.rtol)).sum()
+                dist.all_reduce(bad)
+                say(f"  vs the serving-operator path {name}: violations {int(bad)}/"
+                    f"{got[c].numel() * world} (reported, not asserted)")
         o_row = None
         if args.o_proj:
             # Q as the attention output; the reference side is an NCCL
@@ -265,17 +330,27 @@ def main(args):
         say(f"  ours   : {ours:.3f} ms | GEMM-equivalent {flops / (ours * 1e9):.2f} TFLOP/s")
         say(f"  PyTorch: {ref:.3f} ms | GEMM-equivalent {flops / (ref * 1e9):.2f} TFLOP/s")
         say(f"  ours vs PyTorch: {ref / ours:.2f}x")
+        srv = None
+        if serving is not None:
+            srv = timed(lambda: serving(x, positions))
+            say(f"  serving operators (vLLM fused_qk_norm_rope): {srv:.3f} ms | ours vs them: "
+                f"{srv / ours:.2f}x")
         if i > 0:
-            rows.append((L, ours, ref, o_row))
+            rows.append((L, ours, ref, o_row, srv))
     if rows:
         say("\n| Local tokens (L) | ours (ms) | PyTorch+NCCL (ms) | vs PyTorch |")
         say("| ---: | ---: | ---: | ---: |")
-        for L, o, r, _ in rows:
+        for L, o, r, _, _ in rows:
             say(f"| {L} | {o:.3f} | {r:.3f} | {r / o:.2f}x |")
+        if serving is not None:
+            say("\n| Local tokens (L) | ours (ms) | serving operators + NCCL (ms) | ratio |")
+            say("| ---: | ---: | ---: | ---: |")
+            for L, o, _, _, v in rows:
+                say(f"| {L} | {o:.3f} | {v:.3f} | {v / o:.2f}x |")
         if args.o_proj:
             say("\n| Local tokens (L) | o_proj ours (ms) | NCCL all_to_all + cuBLAS (ms) | ratio |")
             say("| ---: | ---: | ---: | ---: |")
-            for L, _, _, (o, r) in rows:
+            for L, _, _, (o, r), _ in rows:
                 say(f"| {L} | {o:.3f} | {r:.3f} | {r / o:.2f}x |")
     ctx.close()
     dist.destroy_process_group(gloo)

@@ -57,10 +57,12 @@ def run_emulated(S, H, q_heads, tokens, attn, w, calls=1, variant=0):
 @pytest.mark.parametrize("S,H,q_heads,tokens", [
     (1, 4096, 32, 1), (1, 4096, 32, 129), (2, 1024, 8, 300), (4, 2048, 16, 1000),
     (8, 1024, 8, 64), (4, 4096, 32, 1024), (2, 512, 2, 1), (8, 4096, 32, 257),
-    (2, 4096, 16, 300), (1, 2048, 16, 8192),
+    (2, 4096, 16, 300), (1, 2048, 16, 8192), (1, 4096, 32, 4096), (2, 4096, 32, 2500),
 ])
 def test_oproj_emulated_groups(S, H, q_heads, tokens):
-    """Tile widths 64 (small L), 128 (L=300 at H=4096) and 256 (large L)."""
+    """Tile widths 64 (small L), 128 (L=300 at H=4096) and 256 (large L);
+    L=4096 and 2500 at H=4096 leave a last round that at most half fills the
+    74 pairs (34 and 12 tiles), re-tiled into 128-column units."""
     attn, w = world_inputs(S, H, q_heads, tokens)
     topo = oracle.Topology(S, S, q_heads, q_heads, H)
     got, gathered = run_emulated(S, H, q_heads, tokens, attn, w)
@@ -80,11 +82,13 @@ def test_oproj_emulated_groups(S, H, q_heads, tokens):
 @pytest.mark.parametrize("S,H,q_heads,tokens,variant", [
     (2, 1024, 8, 300, "single"), (2, 1024, 8, 300, "pair"), (1, 4096, 32, 2000, "single"),
     (1, 4096, 32, 2000, "pair"), (4, 2048, 16, 129, "pair"), (1, 512, 4, 1, "pair"),
+    (1, 4096, 32, 1200, "single"), (1, 4096, 32, 4096, "noretile"),
 ])
 def test_oproj_variants(S, H, q_heads, tokens, variant):
     """The single-CTA and the CTA-pair GEMM (odd m-block counts leave the last
     pair's second CTA without rows), tile widths 64 to 256."""
-    flag = {"single": _C.FU_FWD_SINGLE, "pair": _C.FU_FWD_PAIR}[variant]
+    flag = {"single": _C.FU_FWD_SINGLE, "pair": _C.FU_FWD_PAIR,
+            "noretile": _C.FU_FWD_NO_RETILE}[variant]
     attn, w = world_inputs(S, H, q_heads, tokens, seed=11)
     topo = oracle.Topology(S, S, q_heads, q_heads, H)
     got, _ = run_emulated(S, H, q_heads, tokens, attn, w, variant=flag)
@@ -96,7 +100,7 @@ def test_oproj_variants(S, H, q_heads, tokens, variant):
 
 @pytest.mark.parametrize("S,H,q_heads,tokens", [
     (1, 1024, 8, 65), (2, 512, 4, 300), (4, 1024, 8, 130), (8, 2048, 16, 17),
-    (1, 1024, 8, 600),
+    (1, 1024, 8, 600), (1, 4096, 32, 1200),
 ])
 def test_oproj_bit_exact_on_exact_inputs(S, H, q_heads, tokens):
     """Integer-valued operands: every order of the FP32 sums is exact, so the
