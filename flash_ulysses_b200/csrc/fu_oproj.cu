@@ -91,16 +91,13 @@ struct OprojParams {
     CUtensorMap tm_self;               // this rank's attention output [S * L, cpm]: box {64, 128}
     const __nv_bfloat16* attn;         // this rank's attention output [S * L, cpm]
     __nv_bfloat16* gather[FU_MAX_SP];  // member d's gather buffer [>= L, K]
-    CUtensorMap tm_w;                  // W_o [H, K]: box {64, bn} (pair: bn / 2)
-    CUtensorMap tm_w_half;             // the same with half the rows, for half-width units
+    CUtensorMap tm_w;                  // W_o [H, K]: box {64, bn}
     CUtensorMap tm_out;                // out [L, H]: box {64, 32}
     uint32_t* sync[FU_MAX_SP];         // member d's sync block
     int32_t* status;
     unsigned long long timeout_ns;
     int32_t L, H, K, cpm, sp_size, sp_rank;
     int32_t num_m, num_n, num_tiles, k_blocks, units;
-    int32_t num_units;                 // work units of the persistent grid (see Sched::unit)
-    int32_t full_units;                // units [0, full_units) are whole tiles
     int32_t row_tiles;                        // tile rows (128 rows, or 256 for a pair)
     int32_t col_major;                        // 1: tiles numbered column-major (see Sched)
     int32_t bn;                        // output columns per tile: 256, 128 or 64
@@ -259,19 +256,6 @@ struct Sched {
     __device__ int n_block(const OprojParams& p, int t) const {
         return p.col_major ? t / p.row_tiles : t % p.num_n;
     }
-    // Work unit u: tile t whole (half = -1), or -- in a last, partial round
-    // that at most half fills the grid, re-tiled over twice as many CTAs or
-    // pairs -- the left (half = 0) or right (1) bn / 2 columns of tile t.
-    __device__ void unit(const OprojParams& p, int u, int& t, int& half) const {
-        if (u < p.full_units) {
-            t = u;
-            half = -1;
-        } else {
-            const int j = u - p.full_units;
-            t = p.full_units + (j >> 1);
-            half = j & 1;
-        }
-    }
 };
 
 // ------------------------------------------------------------ producer
@@ -286,22 +270,14 @@ __device__ void run_producer(const OprojParams& p, uint8_t* smem, const Bars& b,
     const int self_kb0 = p.sp_rank * p.cpm / BK;
     const int self_kb1 = self_kb0 + p.cpm / BK;
     const int b_rows = kPair ? p.bn / 2 : p.bn;   // W_o rows this CTA loads per tile
-    const uint32_t half_stage_bytes = A_STAGE_BYTES + (b_rows / 2) * BK * 2;
     int stage = 0;
     uint32_t phase = 0;
     uint32_t issued_mask = 0, last_parity = 0;
     int ready_m = -1;                             // highest m-block known complete
     bool ok = true;
-    for (int u = sc.first; ok && u < p.num_units; u += sc.stride) {
-        int t, half;
-        sc.unit(p, u, t, half);
+    for (int t = sc.first; ok && t < p.num_tiles; t += sc.stride) {
         const int mb = sc.m_block(p, t);
         const int nb = sc.n_block(p, t);
-        // This CTA's rows of W_o for the unit, and the bytes of one stage.
-        const CUtensorMap* tm_w = half < 0 ? &p.tm_w : &p.tm_w_half;
-        const int w_row = half < 0 ? nb * p.bn + sc.rank * b_rows
-                                   : nb * p.bn + half * (p.bn / 2) + sc.rank * (b_rows / 2);
-        const uint32_t bytes = half < 0 ? static_cast<uint32_t>(p.stage_bytes) : half_stage_bytes;
         if (mb > ready_m && target > 0 && mb < p.num_m) {
             // Every source's slices of this m-block have landed in G.
             const uint64_t t0 = globaltimer_ns();
@@ -329,22 +305,23 @@ __device__ void run_producer(const OprojParams& p, uint8_t* smem, const Bars& b,
             if (kPair) {
                 // Both CTAs' bytes are counted on the leader's barrier.
                 const uint32_t full = map_cluster_smem(b.full + 8 * stage, 0);
-                if (sc.rank == 0) mbar_arrive_expect_tx(b.full + 8 * stage, 2 * bytes);
+                if (sc.rank == 0) mbar_arrive_expect_tx(b.full + 8 * stage, 2 * p.stage_bytes);
                 if (ka)
                     tma_load_2d_pair(adst, &p.tm_self, full, (kb - self_kb0) * BK,
                                      p.sp_rank * p.L + mb * BM);
                 else
                     tma_load_2d_pair(adst, &p.tm_g, full, kb * BK, mb * BM);
-                tma_load_2d_pair(adst + A_STAGE_BYTES, tm_w, full, kb * BK, w_row);
+                tma_load_2d_pair(adst + A_STAGE_BYTES, &p.tm_w, full, kb * BK,
+                                 nb * p.bn + sc.rank * b_rows);
             } else {
                 const uint32_t full = b.full + 8 * stage;
-                mbar_arrive_expect_tx(full, bytes);
+                mbar_arrive_expect_tx(full, p.stage_bytes);
                 if (ka)
                     tma_load_2d(adst, &p.tm_self, full, (kb - self_kb0) * BK,
                                 p.sp_rank * p.L + mb * BM);
                 else
                     tma_load_2d(adst, &p.tm_g, full, kb * BK, mb * BM);
-                tma_load_2d(adst + A_STAGE_BYTES, tm_w, full, kb * BK, w_row);
+                tma_load_2d(adst + A_STAGE_BYTES, &p.tm_w, full, kb * BK, nb * p.bn);
             }
             issued_mask |= 1u << stage;
             last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
@@ -376,17 +353,14 @@ template <bool kPair>
 __device__ void run_mma(const OprojParams& p, uint8_t* smem, uint32_t tmem_base, const Bars& b,
                         volatile int* abort_flag) {
     const Sched<kPair> sc;
-    const uint32_t idesc_full = make_idesc_bf16_f32(kPair ? 2 * BM : BM, p.bn,
-                                                    /*a_mn_major=*/false, /*b_mn_major=*/false);
-    const uint32_t idesc_half = make_idesc_bf16_f32(kPair ? 2 * BM : BM, p.bn / 2,
-                                                    /*a_mn_major=*/false, /*b_mn_major=*/false);
+    const uint32_t idesc = make_idesc_bf16_f32(kPair ? 2 * BM : BM, p.bn, /*a_mn_major=*/false,
+                                               /*b_mn_major=*/false);
     const uint32_t ring = smem_u32(smem + OFF_RING);
     int stage = 0;
     uint32_t phase = 0;
     int local = 0;
     bool ok = true;
-    for (int u = sc.first; ok && u < p.num_units; u += sc.stride, ++local) {
-        const uint32_t idesc = u < p.full_units ? idesc_full : idesc_half;
+    for (int t = sc.first; ok && t < p.num_tiles; t += sc.stride, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!fu_wait_parity(b.tempty + 8 * acc, acc_phase ^ 1u, abort_flag, p.timeout_ns,
@@ -457,31 +431,27 @@ __device__ void run_epilogue(const OprojParams& p, uint8_t* smem, uint32_t tmem_
     const uint32_t swz_row = lane * 128;
     const int swz = lane & 7;
     int local = 0;
-    for (int u = sc.first; u < p.num_units; u += sc.stride, ++local) {
-        int t, half;
-        sc.unit(p, u, t, half);
+    for (int t = sc.first; t < p.num_tiles; t += sc.stride, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         const int mb = sc.m_block(p, t);
-        // First output column and width of the unit.
-        const int col0 = sc.n_block(p, t) * p.bn + (half < 0 ? 0 : half * (p.bn / 2));
-        const int width = half < 0 ? p.bn : p.bn / 2;
+        const int nb = sc.n_block(p, t);
         if (!fu_wait_parity(b.tfull + 8 * acc, acc_phase, abort_flag, p.timeout_ns, p.status,
                             W_TFULL))
             break;
         tc_fence_after();
         const uint32_t acc_addr = tmem_base + lane_addr + acc * BN;
-        // width / 64 boxes of 64 columns, two at a time through the warp's staging.
-        const int boxes = width / 64;
+        // bn / 64 boxes of 64 columns, two at a time through the warp's staging.
+        const int boxes = p.bn / 64;
 #pragma unroll 1
-        for (int half_box = 0; half_box < (boxes + 1) / 2; ++half_box) {
+        for (int half = 0; half < (boxes + 1) / 2; ++half) {
             if (lane == 0) bulk_wait_read_all();  // the staging was read by the last store
             __syncwarp();
 #pragma unroll
             for (int bx = 0; bx < 2; ++bx) {
-                if (half_box * 2 + bx >= boxes) break;
+                if (half * 2 + bx >= boxes) break;
                 uint8_t* box = box0 + bx * BOX_BYTES;
-                const int c0 = (half_box * 2 + bx) * 64;
+                const int c0 = (half * 2 + bx) * 64;
 #pragma unroll
                 for (int c = 0; c < 64; c += 32) {
                     uint32_t r[32];
@@ -504,9 +474,9 @@ __device__ void run_epilogue(const OprojParams& p, uint8_t* smem, uint32_t tmem_
             if (lane == 0) {
                 // Rows past L are clipped by the tensor map.
                 const int row = mb * BM + quarter * 32;
-                for (int bx = 0; bx < 2 && half_box * 2 + bx < boxes; ++bx)
+                for (int bx = 0; bx < 2 && half * 2 + bx < boxes; ++bx)
                     tma_store_2d(&p.tm_out, smem_u32(box0 + bx * BOX_BYTES),
-                                 col0 + (half_box * 2 + bx) * 64, row);
+                                 nb * p.bn + (half * 2 + bx) * 64, row);
                 bulk_commit_group();
             }
         }
@@ -803,9 +773,6 @@ extern "C" int fu_oproj_forward(fu_oproj_ctx* ctx, const void* attn, const void*
         if (rc == FU_OK) rc = encode_2d(&p.tm_self, attn, S * L, cpm, oproj::BM, "attn");
         if (rc == FU_OK)
             rc = encode_2d(&p.tm_w, w_o, H, K, static_cast<uint32_t>(pair ? bn / 2 : bn), "w_o");
-        if (rc == FU_OK)
-            rc = encode_2d(&p.tm_w_half, w_o, H, K, static_cast<uint32_t>(pair ? bn / 4 : bn / 2),
-                           "w_o");
         if (rc == FU_OK) rc = encode_2d(&p.tm_out, out, L, H, 32, "out");
         if (rc != FU_OK) return rc;
     }
@@ -832,18 +799,6 @@ extern "C" int fu_oproj_forward(fu_oproj_ctx* ctx, const void* attn, const void*
     p.row_tiles = static_cast<int32_t>(row_tiles);
     p.col_major = S == 1 ? 1 : 0;
     p.num_tiles = do_gemm ? static_cast<int32_t>(row_tiles) * p.num_n : 0;
-    // Whole tiles fill the full rounds of the grid; a last, partial round that
-    // at most half fills it is re-tiled into half-width units (bn / 2 columns)
-    // over twice as many CTAs or pairs, so it takes about half a round.
-    p.num_units = p.num_tiles;
-    p.full_units = p.num_tiles;
-    {
-        const int64_t rem = p.num_tiles % slots;
-        if (rem > 0 && 2 * rem <= slots && bn >= 128 && (flags & FU_FWD_NO_RETILE) == 0) {
-            p.full_units = static_cast<int32_t>(p.num_tiles - rem);
-            p.num_units = static_cast<int32_t>(p.num_tiles + rem);
-        }
-    }
     p.k_blocks = static_cast<int32_t>(K / oproj::BK);
     // Push units of ~32 KiB: 8 to 128 rows (a power of two) of cpm columns.
     int slice_rows = 8;
@@ -856,10 +811,10 @@ extern "C" int fu_oproj_forward(fu_oproj_ctx* ctx, const void* attn, const void*
     p.do_gemm = do_gemm ? 1u : 0u;
     int grid;
     if (pair) {
-        // One pair per unit up to the co-resident pairs (push units ride along).
-        grid = 2 * static_cast<int>(p.num_units < ctx->max_pairs ? p.num_units : ctx->max_pairs);
+        // One pair per tile up to the co-resident pairs (push units ride along).
+        grid = 2 * static_cast<int>(p.num_tiles < ctx->max_pairs ? p.num_tiles : ctx->max_pairs);
     } else {
-        const int64_t work = p.num_units > p.units ? p.num_units : p.units;
+        const int64_t work = p.num_tiles > p.units ? p.num_tiles : p.units;
         // At least one CTA, which advances the epoch (a push-only call of a
         // world of one has nothing else to do).
         grid = static_cast<int>(work < 1 ? 1 : work < ctx->sm_count ? work : ctx->sm_count);

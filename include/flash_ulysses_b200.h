@@ -98,10 +98,9 @@ enum fu_device_status {
  * CTA pairs (tcgen05 cta_group::2) on 256 x 256 tiles. */
 #define FU_FWD_SINGLE (1u << 12)
 #define FU_FWD_PAIR (2u << 12)
-/* Keep whole tiles in the last round of the persistent grid.  By default a
- * last round that at most half fills the grid is re-tiled into half-width
- * units over twice as many CTAs or pairs: one-head units in fu_qkv_forward's
- * pair grid, bn / 2-column units in fu_oproj_forward's GEMM. */
+/* Keep whole 2-head tiles in the last round of the pair grid (by default a
+ * last round that at most half fills the pairs is re-tiled into one-head
+ * units). */
 #define FU_FWD_NO_RETILE (1u << 14)
 /* Keep Q/K in FP32 from the accumulator through RMSNorm and RoPE and round to
  * BF16 once at the end -- the numerics of the reference's Hopper kernel
@@ -288,8 +287,8 @@ FU_API int fu_oproj_create(const fu_oproj_topology* topo, fu_oproj_ctx** out);
 FU_API int fu_oproj_destroy(fu_oproj_ctx* ctx);
 
 /* One call, one launch on `stream` (flags: FU_FWD_NO_PEER_WAIT, FU_FWD_SINGLE /
- * FU_FWD_PAIR to force the GEMM variant, FU_FWD_NO_RETILE, FU_FWD_NO_PDL,
- * FU_OPROJ_GATHER_ONLY / FU_OPROJ_GEMM_ONLY):
+ * FU_FWD_PAIR to force the GEMM variant, FU_FWD_NO_PDL, FU_OPROJ_GATHER_ONLY /
+ * FU_OPROJ_GEMM_ONLY):
  *   attn   BF16 [S * local_tokens, q_heads/S * 128], this rank's attention output
  *   w_o    BF16 [H, q_heads * 128]
  *   out    BF16 [local_tokens, H]

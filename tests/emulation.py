@@ -137,8 +137,7 @@ class EmulatedOprojGroup:
             self.ops.append(_C.OprojOp(t))
 
     def run(self, attn_outs, weights, outs, tokens, variant=0):
-        """``variant``: 0 automatic, or FU_FWD_SINGLE / FU_FWD_PAIR for the GEMM
-        (and FU_FWD_NO_RETILE to keep whole tiles in its last round)."""
+        """``variant``: 0 automatic, or FU_FWD_SINGLE / FU_FWD_PAIR for the GEMM."""
         stream = _C.current_stream_handle(self.device.index or 0)
         base = _C.FU_FWD_NO_PEER_WAIT
         for r in range(self.S):

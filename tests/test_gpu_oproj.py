@@ -61,8 +61,8 @@ def run_emulated(S, H, q_heads, tokens, attn, w, calls=1, variant=0):
 ])
 def test_oproj_emulated_groups(S, H, q_heads, tokens):
     """Tile widths 64 (small L), 128 (L=300 at H=4096) and 256 (large L);
-    L=4096 and 2500 at H=4096 leave a last round that at most half fills the
-    74 pairs (34 and 12 tiles), re-tiled into 128-column units."""
+    L=4096 and 2500 at H=4096 leave a last round that fills 34 and 12 of the
+    74 pairs."""
     attn, w = world_inputs(S, H, q_heads, tokens)
     topo = oracle.Topology(S, S, q_heads, q_heads, H)
     got, gathered = run_emulated(S, H, q_heads, tokens, attn, w)
@@ -82,13 +82,12 @@ def test_oproj_emulated_groups(S, H, q_heads, tokens):
 @pytest.mark.parametrize("S,H,q_heads,tokens,variant", [
     (2, 1024, 8, 300, "single"), (2, 1024, 8, 300, "pair"), (1, 4096, 32, 2000, "single"),
     (1, 4096, 32, 2000, "pair"), (4, 2048, 16, 129, "pair"), (1, 512, 4, 1, "pair"),
-    (1, 4096, 32, 1200, "single"), (1, 4096, 32, 4096, "noretile"),
+    (1, 4096, 32, 1200, "single"),
 ])
 def test_oproj_variants(S, H, q_heads, tokens, variant):
     """The single-CTA and the CTA-pair GEMM (odd m-block counts leave the last
     pair's second CTA without rows), tile widths 64 to 256."""
-    flag = {"single": _C.FU_FWD_SINGLE, "pair": _C.FU_FWD_PAIR,
-            "noretile": _C.FU_FWD_NO_RETILE}[variant]
+    flag = {"single": _C.FU_FWD_SINGLE, "pair": _C.FU_FWD_PAIR}[variant]
     attn, w = world_inputs(S, H, q_heads, tokens, seed=11)
     topo = oracle.Topology(S, S, q_heads, q_heads, H)
     got, _ = run_emulated(S, H, q_heads, tokens, attn, w, variant=flag)

@@ -113,14 +113,11 @@ def test_push_unit_sizes():
 
 @settings(max_examples=150, deadline=None)
 @given(st.integers(1, 9000), st.sampled_from([256, 512, 1024, 2048, 4096, 8192]),
-       st.integers(1, 74), st.booleans(), st.booleans(), st.booleans())
-def test_oproj_tiles_cover_the_output_once(L, H, pairs, pair, col_major, retile):
-    """fu_oproj_forward's tiling, its re-tiled last round and
-    Sched<kPair>::unit / m_block / n_block (tiles numbered row by row with
-    peers, column by column for a world of one): every (row, column) block of
-    64 output columns of out [L, H] is stored by exactly one CTA, and a CTA's
-    m-blocks never decrease along its walk with peers (the producer's
-    ready-counter wait relies on it)."""
+       st.integers(1, 74), st.booleans(), st.booleans())
+def test_oproj_tiles_cover_the_output_once(L, H, pairs, pair, col_major):
+    """fu_oproj_forward's tiling and Sched<kPair>::m_block / n_block (tiles
+    numbered row by row with peers, column by column for a world of one):
+    every (row block, column block) of out [L, H] is stored by exactly one CTA."""
     num_m = (L + BM - 1) // BM
     row_tiles = (L + 2 * BM - 1) // (2 * BM) if pair else num_m
     slots = pairs if pair else 148
@@ -131,30 +128,14 @@ def test_oproj_tiles_cover_the_output_once(L, H, pairs, pair, col_major, retile)
             break
     num_n = H // bn
     tiles = row_tiles * num_n
-    units, full = tiles, tiles
-    rem = tiles % slots
-    if retile and rem > 0 and 2 * rem <= slots and bn >= 128:
-        full, units = tiles - rem, tiles + rem
     stored = Counter()
-    ctas = 2 * min(units, pairs) if pair else min(units, 148)
+    ctas = 2 * min(tiles, pairs) if pair else min(tiles, 148)
     for cta in range(ctas):
         rank = cta % 2 if pair else 0
         first, stride = (cta // 2, ctas // 2) if pair else (cta, ctas)
-        last_mb = -1
-        for u in range(first, units, stride):
-            if u < full:
-                t, half = u, -1
-            else:
-                t, half = full + (u - full) // 2, (u - full) % 2
+        for t in range(first, tiles, stride):
             mt, nb = (t % row_tiles, t // row_tiles) if col_major else divmod(t, num_n)
             mb = 2 * mt + rank if pair else mt
-            if not col_major:
-                assert mb >= last_mb
-                last_mb = mb
-            col0 = nb * bn + (0 if half < 0 else half * bn // 2)
-            width = bn if half < 0 else bn // 2
-            assert width % 64 == 0
             if mb < num_m:                        # a pair's second CTA may have no rows
-                for c in range(col0, col0 + width, 64):
-                    stored[(mb, c)] += 1
-    assert stored == Counter({(m, c): 1 for m in range(num_m) for c in range(0, H, 64)})
+                stored[(mb, nb)] += 1
+    assert stored == Counter({(m, n): 1 for m in range(num_m) for n in range(num_n)})
