@@ -126,11 +126,6 @@ __device__ __forceinline__ float round_if(float v, bool to_bf16) {
     return to_bf16 ? bf16_round(v) : v;
 }
 
-// Both values rounded to BF16 and back (one packed conversion).
-__device__ __forceinline__ float2 round2_bf16(float2 v) {
-    return __bfloat1622float2(__floats2bfloat162_rn(v.x, v.y));
-}
-
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
     __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&u);
     return __bfloat1622float2(b);
@@ -562,9 +557,7 @@ __device__ __forceinline__ void emit_head(const QkvParams& p, uint32_t taddr, in
         // accumulators are added in order k = 0..3 (into lane[l]) and then the
         // lanes l = 0..7 left to right.  One accumulator at a time keeps only
         // the eight lane sums live next to the cos|sin registers.
-        // Lanes 2j and 2j+1 travel as one pair through the packed FP32
-        // operations (each half rounded on its own, as the scalar ones).
-        float2 lane2[4];
+        float lane[8];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             uint32_t r[4][8];
@@ -572,26 +565,21 @@ __device__ __forceinline__ void emit_head(const QkvParams& p, uint32_t taddr, in
             for (int c = 0; c < 4; ++c) tmem_ld_8cols(taddr + 32 * c + 8 * k, r[c]);
             tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                float2 acc = make_float2(0.f, 0.f);
+            for (int l = 0; l < 8; ++l) {
+                float acc = 0.f;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    float2 f = make_float2(__uint_as_float(r[c][2 * j]),
-                                           __uint_as_float(r[c][2 * j + 1]));
-                    if (!p.fp32_epilogue) f = round2_bf16(f);
-                    const float2 sq = __fmul2_rn(f, f);
-                    acc = c == 0 ? sq : __fadd2_rn(acc, sq);
+                    float f = __uint_as_float(r[c][l]);
+                    if (!p.fp32_epilogue) f = bf16_round(f);
+                    const float sq = __fmul_rn(f, f);
+                    acc = c == 0 ? sq : __fadd_rn(acc, sq);
                 }
-                lane2[j] = k == 0 ? acc : __fadd2_rn(lane2[j], acc);
+                lane[l] = k == 0 ? acc : __fadd_rn(lane[l], acc);
             }
         }
-        float ss = lane2[0].x;
-        ss = __fadd_rn(ss, lane2[0].y);
+        float ss = lane[0];
 #pragma unroll
-        for (int j = 1; j < 4; ++j) {
-            ss = __fadd_rn(ss, lane2[j].x);
-            ss = __fadd_rn(ss, lane2[j].y);
-        }
+        for (int l = 1; l < 8; ++l) ss = __fadd_rn(ss, lane[l]);
         const float eps = comp == 0 ? p.q_eps : p.k_eps;
         scale = norm_scale(ss, eps);
     }
@@ -610,15 +598,11 @@ __device__ __forceinline__ void emit_head(const QkvParams& p, uint32_t taddr, in
         tmem_ld_wait();
         // The projection as the epilogue sees it: rounded to BF16 (reference
         // PyTorch path) or the FP32 accumulator (FP32-intermediate mode).
-        float2 lo2[8], hi2[8];
+        float lo_v[16], hi_v[16];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            lo2[i] = make_float2(__uint_as_float(lo_raw[2 * i]), __uint_as_float(lo_raw[2 * i + 1]));
-            hi2[i] = make_float2(__uint_as_float(hi_raw[2 * i]), __uint_as_float(hi_raw[2 * i + 1]));
-            if (r16) {
-                lo2[i] = round2_bf16(lo2[i]);
-                hi2[i] = round2_bf16(hi2[i]);
-            }
+        for (int i = 0; i < 16; ++i) {
+            lo_v[i] = round_if(__uint_as_float(lo_raw[i]), r16);
+            hi_v[i] = round_if(__uint_as_float(hi_raw[i]), r16);
         }
         if (p.gemm_out != nullptr && row_valid) {
             __nv_bfloat16* row = p.gemm_out + static_cast<int64_t>(m) * p.N + h * 128;
@@ -626,53 +610,62 @@ __device__ __forceinline__ void emit_head(const QkvParams& p, uint32_t taddr, in
             uint4* dhi = reinterpret_cast<uint4*>(row + 64 + 16 * q);
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
-                dlo[c] = make_uint4(pack_bf16x2(lo2[4 * c].x, lo2[4 * c].y),
-                                    pack_bf16x2(lo2[4 * c + 1].x, lo2[4 * c + 1].y),
-                                    pack_bf16x2(lo2[4 * c + 2].x, lo2[4 * c + 2].y),
-                                    pack_bf16x2(lo2[4 * c + 3].x, lo2[4 * c + 3].y));
-                dhi[c] = make_uint4(pack_bf16x2(hi2[4 * c].x, hi2[4 * c].y),
-                                    pack_bf16x2(hi2[4 * c + 1].x, hi2[4 * c + 1].y),
-                                    pack_bf16x2(hi2[4 * c + 2].x, hi2[4 * c + 2].y),
-                                    pack_bf16x2(hi2[4 * c + 3].x, hi2[4 * c + 3].y));
+                dlo[c] = make_uint4(pack_bf16x2(lo_v[8 * c], lo_v[8 * c + 1]),
+                                    pack_bf16x2(lo_v[8 * c + 2], lo_v[8 * c + 3]),
+                                    pack_bf16x2(lo_v[8 * c + 4], lo_v[8 * c + 5]),
+                                    pack_bf16x2(lo_v[8 * c + 6], lo_v[8 * c + 7]));
+                dhi[c] = make_uint4(pack_bf16x2(hi_v[8 * c], hi_v[8 * c + 1]),
+                                    pack_bf16x2(hi_v[8 * c + 2], hi_v[8 * c + 3]),
+                                    pack_bf16x2(hi_v[8 * c + 4], hi_v[8 * c + 5]),
+                                    pack_bf16x2(hi_v[8 * c + 6], hi_v[8 * c + 7]));
             }
         }
         uint32_t olo[8], ohi[8];
         if (comp < 2) {
+            const float cs[16] = {cosv[4 * q].x, cosv[4 * q].y, cosv[4 * q].z, cosv[4 * q].w,
+                                  cosv[4 * q + 1].x, cosv[4 * q + 1].y, cosv[4 * q + 1].z,
+                                  cosv[4 * q + 1].w, cosv[4 * q + 2].x, cosv[4 * q + 2].y,
+                                  cosv[4 * q + 2].z, cosv[4 * q + 2].w, cosv[4 * q + 3].x,
+                                  cosv[4 * q + 3].y, cosv[4 * q + 3].z, cosv[4 * q + 3].w};
+            const float sn[16] = {sinv[4 * q].x, sinv[4 * q].y, sinv[4 * q].z, sinv[4 * q].w,
+                                  sinv[4 * q + 1].x, sinv[4 * q + 1].y, sinv[4 * q + 1].z,
+                                  sinv[4 * q + 1].w, sinv[4 * q + 2].x, sinv[4 * q + 2].y,
+                                  sinv[4 * q + 2].z, sinv[4 * q + 2].w, sinv[4 * q + 3].x,
+                                  sinv[4 * q + 3].y, sinv[4 * q + 3].z, sinv[4 * q + 3].w};
             // Gamma for columns 16q.. and 64+16q.. (same address in every lane: a
             // broadcast, read as 16-byte vectors).
-            const float4* gl4 = reinterpret_cast<const float4*>(g + 16 * q);
-            const float4* gh4 = reinterpret_cast<const float4*>(g + 64 + 16 * q);
-            const float2 sc2 = make_float2(scale, scale);
+            float gl[16], gh[16];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float4 a = reinterpret_cast<const float4*>(g + 16 * q)[i];
+                const float4 b4 = reinterpret_cast<const float4*>(g + 64 + 16 * q)[i];
+                gl[4 * i] = a.x; gl[4 * i + 1] = a.y; gl[4 * i + 2] = a.z; gl[4 * i + 3] = a.w;
+                gh[4 * i] = b4.x; gh[4 * i + 1] = b4.y; gh[4 * i + 2] = b4.z; gh[4 * i + 3] = b4.w;
+            }
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                // Columns 2i, 2i+1 of this group of 16: float4 element i/2, half i%2.
-                const float4 ga = gl4[i >> 1], gb = gh4[i >> 1];
-                const float4 c4 = cosv[4 * q + (i >> 1)], s4 = sinv[4 * q + (i >> 1)];
-                const bool upper = (i & 1) != 0;
-                const float2 glo = upper ? make_float2(ga.z, ga.w) : make_float2(ga.x, ga.y);
-                const float2 ghi = upper ? make_float2(gb.z, gb.w) : make_float2(gb.x, gb.y);
-                const float2 c2 = upper ? make_float2(c4.z, c4.w) : make_float2(c4.x, c4.y);
-                const float2 s2 = upper ? make_float2(s4.z, s4.w) : make_float2(s4.x, s4.y);
                 // RMSNorm, * gamma, BF16 boundary (torch_base.py:56-61).
-                float2 nl = __fmul2_rn(__fmul2_rn(lo2[i], sc2), glo);
-                float2 nh = __fmul2_rn(__fmul2_rn(hi2[i], sc2), ghi);
-                if (r16) {
-                    nl = round2_bf16(nl);
-                    nh = round2_bf16(nh);
-                }
-                // NeoX rotation, separately rounded products (torch_base.py:62-63);
-                // a - b is computed as a + (-b), which rounds identically.
-                const float2 a2 = __fmul2_rn(nl, c2), b2 = __fmul2_rn(nh, s2);
-                const float2 out_lo = __fadd2_rn(a2, make_float2(-b2.x, -b2.y));
-                const float2 out_hi = __fadd2_rn(__fmul2_rn(nh, c2), __fmul2_rn(nl, s2));
-                olo[i] = pack_bf16x2(out_lo.x, out_lo.y);
-                ohi[i] = pack_bf16x2(out_hi.x, out_hi.y);
+                const float nl0 =
+                    round_if(__fmul_rn(__fmul_rn(lo_v[2 * i], scale), gl[2 * i]), r16);
+                const float nl1 =
+                    round_if(__fmul_rn(__fmul_rn(lo_v[2 * i + 1], scale), gl[2 * i + 1]), r16);
+                const float nh0 =
+                    round_if(__fmul_rn(__fmul_rn(hi_v[2 * i], scale), gh[2 * i]), r16);
+                const float nh1 =
+                    round_if(__fmul_rn(__fmul_rn(hi_v[2 * i + 1], scale), gh[2 * i + 1]), r16);
+                // NeoX rotation, separately rounded products (torch_base.py:62-63).
+                const float c0 = cs[2 * i], c1 = cs[2 * i + 1];
+                const float s0 = sn[2 * i], s1 = sn[2 * i + 1];
+                olo[i] = pack_bf16x2(__fsub_rn(__fmul_rn(nl0, c0), __fmul_rn(nh0, s0)),
+                                     __fsub_rn(__fmul_rn(nl1, c1), __fmul_rn(nh1, s1)));
+                ohi[i] = pack_bf16x2(__fadd_rn(__fmul_rn(nh0, c0), __fmul_rn(nl0, s0)),
+                                     __fadd_rn(__fmul_rn(nh1, c1), __fmul_rn(nl1, s1)));
             }
         } else {
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                olo[i] = pack_bf16x2(lo2[i].x, lo2[i].y);
-                ohi[i] = pack_bf16x2(hi2[i].x, hi2[i].y);
+                olo[i] = pack_bf16x2(lo_v[2 * i], lo_v[2 * i + 1]);
+                ohi[i] = pack_bf16x2(hi_v[2 * i], hi_v[2 * i + 1]);
             }
         }
         // 16-byte chunks 2q and 2q+1 of the row in each box (128-byte swizzle).
