@@ -31,6 +31,7 @@ FU_FWD_PAIR = 2 << 12
 FU_FWD_NO_RETILE = 1 << 14
 FU_FWD_FP32_EPILOGUE = 1 << 15
 FU_FWD_NO_PDL = 1 << 17
+FU_FWD_STATIC_WEIGHTS = 1 << 18
 FU_OPROJ_READY = FU_SYNC_WORDS
 FU_OPROJ_GATHER_ONLY = 1 << 20
 FU_OPROJ_GEMM_ONLY = 1 << 21

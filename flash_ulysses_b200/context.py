@@ -197,6 +197,7 @@ class FlashUlyssesContext:
         q_epsilon=1e-6,
         k_epsilon=1e-6,
         check=False,
+        static_weights=False,
         _projection_out=None,
     ):
         """Return BF16 (q, k, v), each with L * sp_size rows.
@@ -213,6 +214,13 @@ class FlashUlyssesContext:
         learns that these outputs are invalid; by default errors surface on
         the next call or ``check()``, without a synchronisation per call.
 
+        ``static_weights=True`` is the caller's promise that no kernel that
+        may still be running on the current stream writes ``qkv_weight``
+        (inference, where weights do not change): the first stages of the
+        weight are then read while the previous kernel finishes, which
+        shortens decode-sized calls.  Results are the same; without the
+        promise holding, a call may read stale weights.
+
         ``_projection_out`` is test instrumentation: a BF16 [L, packed_width]
         tensor that also receives this rank's BF16 projection ``x @ W``.
         """
@@ -224,6 +232,7 @@ class FlashUlyssesContext:
                                + _C.decode_status(self._status.value))
         _C.launch(hidden_states, qkv_weight, positions, q_norm_weight, k_norm_weight,
                   rope_cache, self._op, q_epsilon=q_epsilon, k_epsilon=k_epsilon,
+                  flags=_C.FU_FWD_STATIC_WEIGHTS if static_weights else 0,
                   gemm_out=_projection_out)
         if check:
             torch.cuda.current_stream(self.device).synchronize()

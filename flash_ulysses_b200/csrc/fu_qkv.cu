@@ -115,6 +115,7 @@ struct __align__(64) QkvParams {
     int32_t num_units;                      // work units of the persistent grid
     int32_t full_units;                     // units [0, full_units) are whole tiles; each later
                                             // pair of units is one tile's two heads
+    int32_t static_weights;                 // 1: W may be read before the dependency wait
 };
 static_assert(sizeof(QkvParams) <= 4096, "kernel parameter block too large");
 
@@ -340,6 +341,34 @@ __device__ __forceinline__ bool wait_peers_entered(const QkvParams& p, uint32_t 
 }
 
 // ------------------------------------------------------------ roles
+// Stages of the first work item whose W the prologue loads before the
+// dependency wait (static weights, one-CTA tiles: single or split mode).
+template <bool kPair>
+__device__ __forceinline__ int early_w_stages(const QkvParams& p, const Sched& sc) {
+    if (kPair || !p.static_weights || sc.first >= sc.end) return 0;
+    return min(Ring<kPair>::STAGES, sc.kb1 - sc.kb0);
+}
+
+// The prologue's part of those stages: each stage's barrier is armed with
+// the whole stage's bytes and W's four chunks are requested; the producer
+// adds X after the dependency wait.
+template <bool kPair>
+__device__ __forceinline__ void load_early_w(const QkvParams& p, const Sched& sc, uint8_t* smem,
+                                             const Bars& b) {
+    using R = Ring<kPair>;
+    const int n = early_w_stages<kPair>(p, sc);
+    if (n == 0) return;
+    const int col0 = decode_unit(p, sc.first).n_blk * BN;
+    const uint32_t b0 = smem_u32(smem + R::OFF_B);
+    for (int s = 0; s < n; ++s) {
+        const uint32_t full = b.full + 8 * s;
+        mbar_arrive_expect_tx(full, R::STAGE_TX);
+        for (int c = 0; c < R::B_CHUNKS; ++c)
+            tma_load_2d(b0 + s * R::B_STAGE_BYTES + c * B_CHUNK_BYTES, &p.tm_w, full,
+                        col0 + c * 64, (sc.kb0 + s) * BK);
+    }
+}
+
 template <bool kPair>
 __device__ void run_producer(const QkvParams& p, const Sched& sc, uint8_t* smem, const Bars& b,
                              volatile int* abort_flag) {
@@ -351,6 +380,15 @@ __device__ void run_producer(const QkvParams& p, const Sched& sc, uint8_t* smem,
     const uint32_t a0 = smem_u32(smem + OFF_A);
     const uint32_t b0 = smem_u32(smem + R::OFF_B);
     bool ok = true;
+    // Stages whose W the prologue requested: their X, now that the previous
+    // kernel of the stream has completed (their barriers already expect it).
+    int early = early_w_stages<kPair>(p, sc);
+    if (early > 0) {
+        const int row0 = decode_unit(p, sc.first).m_blk * sc.rows_per_tile;
+        for (int s = 0; s < early; ++s)
+            tma_load_2d(a0 + s * A_STAGE_BYTES, &p.tm_x, b.full + 8 * s, (sc.kb0 + s) * BK, row0);
+        issued_mask = (1u << early) - 1u;
+    }
     Walk walk = make_walk(p, sc);
     Item it;
     while (ok && next_item(p, sc, walk, it)) {
@@ -364,6 +402,14 @@ __device__ void run_producer(const QkvParams& p, const Sched& sc, uint8_t* smem,
         const uint32_t stage_tx = kPair ? 2u * (A_STAGE_BYTES + chunks * B_CHUNK_BYTES)
                                         : R::STAGE_TX;
         for (int kb = it.kb0; kb < it.kb1; ++kb) {
+            if (early > 0) {                        // loaded above (first item, first stages)
+                --early;
+                if (++stage == R::STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+                continue;
+            }
             if (*abort_flag || !fu_wait_parity(b.empty + 8 * stage, phase ^ 1u, abort_flag,
                                                p.timeout_ns, p.status, W_EMPTY)) {
                 ok = false;
@@ -1115,6 +1161,10 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
         fence_mbar_init();
         tma_prefetch_desc(&p.tm_x);
         tma_prefetch_desc(&p.tm_w);
+        // Static weights (the caller's promise that no kernel still running on
+        // the stream writes W): the first stages' W streams in while the
+        // previous kernel finishes.  X and everything else wait for it.
+        load_early_w<kPair>(p, sc, smem, b);
     }
     if (warp == 1) {
         if (kPair) {
@@ -1567,6 +1617,7 @@ extern "C" int fu_qkv_forward(fu_qkv_ctx* ctx, const void* x, const void* w,
     ++ctx->epoch;                                // calls launched (the device keeps the epoch)
     p.wait_peers = (flags & FU_FWD_NO_PEER_WAIT) ? 0u : 1u;
     p.fp32_epilogue = (flags & FU_FWD_FP32_EPILOGUE) ? 1u : 0u;
+    p.static_weights = (flags & FU_FWD_STATIC_WEIGHTS) ? 1 : 0;
 
     p.splits = choose_splits(ctx, tiles, p.k_blocks, L < BM ? L : BM,
                              static_cast<int>((flags >> 8) & 0xFu));

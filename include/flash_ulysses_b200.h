@@ -111,9 +111,19 @@ enum fu_device_status {
  * launched with cudaLaunchAttributeProgrammaticStreamSerialization: its
  * prologue (barrier set-up, TMEM allocation) may run while the previous
  * kernel of the stream finishes, and it reads or writes no global memory
- * before that kernel has completed; it also lets the next such kernel of the
+ * before that kernel has completed (except qkv_weight under
+ * FU_FWD_STATIC_WEIGHTS); it also lets the next such kernel of the
  * stream start its prologue early.  Results are the same either way. */
 #define FU_FWD_NO_PDL (1u << 17)
+/* The caller promises that no kernel that may still be running on the stream
+ * when this call starts writes qkv_weight (inference: weights do not change
+ * between calls).  The first operand stages of W are then requested before
+ * the wait for the previous kernel, so under programmatic dependent launch
+ * they stream in while it finishes (one-CTA tiles: split-K and single-CTA
+ * variants; ignored by the CTA-pair variant).  Inputs written by earlier
+ * kernels (hidden_states, positions, ...) are still read after that wait.
+ * Without the promise holding, the call may read stale weights. */
+#define FU_FWD_STATIC_WEIGHTS (1u << 18)
 
 FU_API const char* fu_last_error(void);
 FU_API int fu_version(void);

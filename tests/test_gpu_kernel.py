@@ -229,6 +229,59 @@ def test_persistent_variants(tokens, variant):
     check_group(run_group(cfg, tokens, splits=1, variant=flag))
 
 
+@pytest.mark.parametrize("tokens,splits,variant", [
+    (1, 0, 0), (1, 3, 0), (4, 0, 0), (64, 0, 0), (129, 5, 0), (300, 1, "single"),
+    (1024, 1, "single"), (300, 1, "pair"),
+])
+def test_static_weights_early_loads(tokens, splits, variant):
+    """FU_FWD_STATIC_WEIGHTS: the first stages of W are requested before the
+    dependency wait (split-K and single-CTA tiles; the pair variant ignores
+    the flag).  Ranks of the emulated group run back to back on one stream,
+    so each call's early loads overlap the previous call; the results meet
+    the same criterion as every other case."""
+    base = CONFIGS["c1"]
+    cfg = base.__class__("c1_p2", 2, 2, base.hidden_size, base.num_heads, base.num_kv_heads,
+                         base.tokens, base.max_position)
+    flag = _C.FU_FWD_STATIC_WEIGHTS | {0: 0, "single": _C.FU_FWD_SINGLE,
+                                       "pair": _C.FU_FWD_PAIR}[variant]
+    check_group(run_group(cfg, tokens, splits=splits, variant=flag))
+
+
+def test_static_weights_context_back_to_back():
+    """The context keyword, calls back to back with a different weight each
+    call (rotating inputs, no synchronisation between them): equal bit for bit
+    to the same calls without the keyword."""
+    from flash_ulysses_b200 import FlashUlyssesContext
+
+    base = CONFIGS["c1"]
+    cfg = base.__class__("c1_p1", 1, 1, base.hidden_size, base.num_heads, base.num_kv_heads,
+                         base.tokens, base.max_position)
+    torch.cuda.set_device(0)
+    ctx = FlashUlyssesContext(rank=0, world_size=1, max_local_tokens=64, hidden_size=4096,
+                              num_heads=32, num_kv_heads=8, sp_size=1)
+    try:
+        for tokens in (1, 5, 64):
+            sets = []
+            for seed in range(3):
+                xs, pos, params = make_world(cfg, tokens, seed=100 + seed)
+                sets.append((xs[0].cuda(), pos[0].cuda(), to_device(params[0], "cuda")))
+            results = {}
+            for static in (False, True):
+                outs = []
+                for i in range(6):
+                    x, p, prm = sets[i % 3]
+                    q, k, v = ctx.ulysses_qkv_forward(x, positions=p, static_weights=static,
+                                                      **prm)
+                    outs.append(tuple(t.clone() for t in (q, k, v)))
+                torch.cuda.synchronize()
+                ctx.check()
+                results[static] = outs
+            for a, b in zip(results[False], results[True]):
+                assert all(torch.equal(u, w) for u, w in zip(a, b)), tokens
+    finally:
+        ctx.close()
+
+
 @pytest.mark.parametrize("cfg_name,tokens,tp_rank,variant", [
     ("c3", 300, 1, "pair"), ("c1", 257, 0, "pair"), ("c0", 130, 0, "pair"),
 ])
