@@ -712,11 +712,12 @@ def main():
             s_sets = sets if L == tokens else [make_inputs(n, rank, L, seed=s)
                                                for s in range(ROTATE)]
 
-            def s_call(i, s_sets=s_sets):
+            def s_call(i, s_sets=s_sets, static=False):
                 x, pos, p = s_sets[i % ROTATE]
                 ctx.ulysses_qkv_forward(x, p["qkv_weight"], pos, p["q_norm_weight"],
                                         p["k_norm_weight"], p["rope_cache"],
-                                        q_epsilon=p["q_epsilon"], k_epsilon=p["k_epsilon"])
+                                        q_epsilon=p["q_epsilon"], k_epsilon=p["k_epsilon"],
+                                        static_weights=static)
 
             s_step = guarded(s_call, failed)
             for i in range(3):
@@ -730,6 +731,16 @@ def main():
                              "grid": ctx._op.last_grid,
                              "weight_read_gbs": round(HIDDEN * ctx.packed_width * 2 / (t * 1e-3)
                                                       / 1e9, 1)}
+            if L <= 128:
+                # The same calls with static_weights=True (inference: no kernel
+                # writes W), whose first weight stages load while the previous
+                # call finishes.
+                st_step = guarded(lambda i, s_sets=s_sets: s_call(i, s_sets, True), failed)
+                for i in range(3):
+                    st_step(i)
+                ts = time_steps(st_step, 200, n, group)
+                healthy(ctx, n, group, f"sweep L={L} static weights")
+                sweep[str(L)]["static_weights_ms"] = round(ts, 5)
             del s_sets
 
     cpu = None
