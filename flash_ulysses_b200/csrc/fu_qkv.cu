@@ -298,9 +298,10 @@ __device__ __forceinline__ int32_t status_at_start(const QkvParams& p) {
         *reinterpret_cast<volatile const uint32_t*>(p.sync[p.sp_rank] + FU_SYNC_FAILED));
 }
 
-// Entry barrier, run by the 4 epilogue warps before their CTA's first store
-// into a peer's buffer: one thread waits (bounded) until every SP member has
-// started this call's epoch, then the warps meet on named barrier 1.  Returns
+// Entry barrier, run before a CTA's first store into a peer's buffer by the 4
+// epilogue warps (or, in the split-K reduction, all six warps: bar_threads):
+// one thread waits (bounded) until every SP member has started this call's
+// epoch, then the warps meet on named barrier 1.  Returns
 // false -- and the CTA stores nothing -- when an earlier call of this operator
 // failed (this queued call must neither wait for peers nor write into them)
 // or when the wait gives up.  Either raises the
@@ -309,7 +310,8 @@ __device__ __forceinline__ int32_t status_at_start(const QkvParams& p) {
 // memory), since the pair's MMAs and accumulator hand-offs involve both.
 __device__ __forceinline__ bool wait_peers_entered(const QkvParams& p, uint32_t epoch,
                                                    volatile int* abort_flag, bool pair,
-                                                   int32_t status_seen) {
+                                                   int32_t status_seen,
+                                                   int bar_threads = NUM_EPI_THREADS) {
     if (threadIdx.x == 64) {
         bool give_up = false;
         if (*abort_flag) {
@@ -336,7 +338,7 @@ __device__ __forceinline__ bool wait_peers_entered(const QkvParams& p, uint32_t 
                                                 cluster_ctarank() ^ 1u), 1u);
         }
     }
-    named_bar_sync(1, NUM_EPI_THREADS);
+    named_bar_sync(1, bar_threads);
     return *abort_flag == 0;
 }
 
@@ -883,7 +885,7 @@ __device__ void run_split_partial(const QkvParams& p, const Sched& sc, uint8_t* 
     }
 }
 
-// Split mode, step 2 (epilogue warps of every cluster CTA, after a cluster
+// Split mode, step 2 (every warp of every cluster CTA, after a cluster
 // barrier): one item = one valid token row x one head.  A warp takes two items
 // at a time; lane l owns columns 4l..4l+3 of the head, loads the partials of
 // every cluster CTA at once (coalesced distributed-shared-memory reads) and
@@ -1013,7 +1015,7 @@ __device__ void run_split_reduce(const QkvParams& p, const Sched& sc, uint8_t* s
         if (any) *abort_flag = 1;
     }
     const int32_t status_seen = *reinterpret_cast<volatile int32_t*>(smem + OFF_MISC + 12);
-    if (!wait_peers_entered(p, epoch, abort_flag, false, status_seen)) return;
+    if (!wait_peers_entered(p, epoch, abort_flag, false, status_seen, NUM_THREADS)) return;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const Unit tile = decode_unit(p, sc.first);
@@ -1022,7 +1024,10 @@ __device__ void run_split_reduce(const QkvParams& p, const Sched& sc, uint8_t* s
     const int rows = min(BM, p.L - m_blk * BM);
     const int heads_here = min(2, p.heads - n_blk * 2);
     const int items = rows * heads_here;
-    const int workers = 4 * p.splits;
+    // Every warp of every cluster CTA takes items: the producer and MMA warps
+    // are idle by now, and each item's chain of shuffles and roundings is
+    // latency-bound, so more warps in flight shorten the reduction.
+    const int workers = NUM_THREADS / 32 * p.splits;
     const uint32_t part = smem_u32(smem + OFF_A);
     const int32_t* rope_rows = reinterpret_cast<const int32_t*>(smem + OFF_STG);
     // Item i: row i / heads_here, head slot i % heads_here.  A warp takes two
@@ -1053,7 +1058,7 @@ __device__ void run_split_reduce(const QkvParams& p, const Sched& sc, uint8_t* s
                 if (r < p.splits) raw.v[k][r] = ld_cluster_f32x4(map_cluster_smem(local, r));
         }
     };
-    const int first = (warp - 2) * p.splits + sc.split;
+    const int first = warp * p.splits + sc.split;
     Raw raw;
     if (first < items) request(first, raw);
     for (int i0 = first; i0 < items; i0 += 2 * workers) {
@@ -1273,7 +1278,7 @@ fused_qkv_exchange_kernel(const __grid_constant__ QkvParams p) {
         // Every CTA of the cluster reaches both barriers on every path, so a
         // CTA that gave up on a wait cannot strand its peers here.
         cluster_sync_all();                 // partials visible cluster-wide
-        if (warp >= 2) run_split_reduce(p, sc, smem, gam, abort_flag, epoch);
+        run_split_reduce(p, sc, smem, gam, abort_flag, epoch);   // all six warps
         cluster_sync_all();                 // peers are done reading this CTA's partial
     }
 
