@@ -1030,38 +1030,54 @@ __device__ void run_split_reduce(const QkvParams& p, const Sched& sc, uint8_t* s
     const int workers = NUM_THREADS / 32 * p.splits;
     const uint32_t part = smem_u32(smem + OFF_A);
     const int32_t* rope_rows = reinterpret_cast<const int32_t*>(smem + OFF_STG);
-    // Item i: row i / heads_here, head slot i % heads_here.  A warp takes
-    // ITEMS items per step (i0, i0 + workers, ...): it requests every cluster
-    // CTA's partial of each and its RoPE values, sums the partials in rank
-    // order (deterministic), then normalises, rotates and stores the items.
-    // Each item is a dependent chain of shuffles and roundings; several
-    // independent ones per step keep the warp busy while any one waits.
-    constexpr int ITEMS = 4;
-    const int first = warp * p.splits + sc.split;
-    for (int i0 = first; i0 < items; i0 += ITEMS * workers) {
-        float4 acc[ITEMS];
-        SplitRope rope[ITEMS];
+    // Item i: row i / heads_here, head slot i % heads_here.  A warp takes two
+    // items per step (i0 and i0 + workers).  Each step first sums the partials
+    // requested by the previous step (in rank order: deterministic), then
+    // requests the next step's partials over distributed shared memory and its
+    // RoPE values, and only then normalises, rotates and stores the current
+    // items, so the remote reads of one step overlap the arithmetic of the
+    // step before.
+    struct Raw {
+        float4 v[2][FU_MAX_SP];
+        SplitRope rope[2];
+    };
+    auto request = [&](int i0, Raw& raw) {
 #pragma unroll
-        for (int k = 0; k < ITEMS; ++k) {
+        for (int k = 0; k < 2; ++k) {
             const int i = min(i0 + k * workers, items - 1);
-            rope[k] = split_item_rope(p, rope_rows, i / heads_here, n_blk * 2 + i % heads_here,
-                                      lane);
+            raw.rope[k] = split_item_rope(p, rope_rows, i / heads_here,
+                                          n_blk * 2 + i % heads_here, lane);
+        }
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int i = min(i0 + k * workers, items - 1);
             const uint32_t local = part + (i / heads_here) * PART_STRIDE +
                                    ((i % heads_here) * 128 + 4 * lane) * 4;
-            float4 v[FU_MAX_SP];
 #pragma unroll
             for (int r = 0; r < FU_MAX_SP; ++r)
-                if (r < p.splits) v[r] = ld_cluster_f32x4(map_cluster_smem(local, r));
-            acc[k] = v[0];
+                if (r < p.splits) raw.v[k][r] = ld_cluster_f32x4(map_cluster_smem(local, r));
+        }
+    };
+    const int first = warp * p.splits + sc.split;
+    Raw raw;
+    if (first < items) request(first, raw);
+    for (int i0 = first; i0 < items; i0 += 2 * workers) {
+        float4 acc[2];
+        SplitRope rope[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            acc[k] = raw.v[k][0];
 #pragma unroll
             for (int r = 1; r < FU_MAX_SP; ++r)
                 if (r < p.splits) {
-                    acc[k].x += v[r].x; acc[k].y += v[r].y;
-                    acc[k].z += v[r].z; acc[k].w += v[r].w;
+                    acc[k].x += raw.v[k][r].x; acc[k].y += raw.v[k][r].y;
+                    acc[k].z += raw.v[k][r].z; acc[k].w += raw.v[k][r].w;
                 }
+            rope[k] = raw.rope[k];
         }
+        if (i0 + 2 * workers < items) request(i0 + 2 * workers, raw);
 #pragma unroll
-        for (int k = 0; k < ITEMS; ++k) {
+        for (int k = 0; k < 2; ++k) {
             const int i = i0 + k * workers;
             if (i < items)
                 split_item_emit(p, acc[k], m_blk * BM + i / heads_here,
