@@ -1076,12 +1076,17 @@ __device__ void run_split_reduce(const QkvParams& p, const Sched& sc, uint8_t* s
             rope[k] = raw.rope[k];
         }
         if (i0 + 2 * workers < items) request(i0 + 2 * workers, raw);
-#pragma unroll
+        // One copy of the item code, looped: the step's code then stays in the
+        // instruction cache (two inlined copies made the warps wait on
+        // instruction fetch for most of each step).
+#pragma unroll 1
         for (int k = 0; k < 2; ++k) {
             const int i = i0 + k * workers;
             if (i < items)
-                split_item_emit(p, acc[k], m_blk * BM + i / heads_here,
-                                n_blk * 2 + i % heads_here, gam, lane, rope[k]);
+                split_item_emit(p, acc[0], m_blk * BM + i / heads_here,
+                                n_blk * 2 + i % heads_here, gam, lane, rope[0]);
+            acc[0] = acc[1];                    // the second item moves up
+            rope[0] = rope[1];
         }
     }
 }
