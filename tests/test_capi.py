@@ -56,6 +56,19 @@ def test_constants_match_header():
         assert m and int(m.group(1)) == getattr(_C, name), name
 
 
+def test_call_flags_match_header():
+    """The per-call flag bits of the binding equal the header's."""
+    text = HEADER.read_text()
+    for name, bit in (("FU_FWD_SINGLE", 12), ("FU_FWD_NO_RETILE", 14),
+                      ("FU_FWD_FP32_EPILOGUE", 15), ("FU_FWD_NO_PDL", 17),
+                      ("FU_FWD_STATIC_WEIGHTS", 18)):
+        assert re.search(rf"#define {name} \(1u << {bit}\)", text), name
+        assert getattr(_C, name) == 1 << bit, name
+    assert re.search(r"#define FU_FWD_PAIR \(2u << 12\)", text) and _C.FU_FWD_PAIR == 2 << 12
+    assert re.search(r"#define FU_FWD_NO_PEER_WAIT 1u", text) and _C.FU_FWD_NO_PEER_WAIT == 1
+    assert all(_C.FU_FWD_SPLITS(n) == (n & 0xF) << 8 for n in range(16))
+
+
 def test_oproj_constants_and_errors_without_gpu():
     text = HEADER.read_text()
     assert re.search(r"#define FU_OPROJ_READY FU_SYNC_WORDS", text)
