@@ -82,12 +82,6 @@ constexpr int SMEM_BYTES = OFF_GAMMA + 2 * 128 * 4;
 // padded by 16 bytes so that a warp's row-per-thread stores spread over banks.
 constexpr int PART_STRIDE = BN * 4 + 16;
 static_assert(BM * PART_STRIDE <= OFF_STG, "split partial must fit in the operand ring");
-// Split mode: one 256-byte output staging row (+16 bytes against bank
-// conflicts) per octet of lanes of the six warps, behind the parked partials.
-constexpr int OFF_OCT = OFF_A + BM * PART_STRIDE;
-constexpr int OCT_STAGE_BYTES = 128 * 2 + 16;
-static_assert(OFF_OCT % 16 == 0 && OFF_OCT + 24 * OCT_STAGE_BYTES <= OFF_STG,
-              "split output staging must fit in the operand ring");
 constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;                 // room to align the base to 1 KiB
 static_assert(NUM_BARS * 8 <= 256, "barrier area");
 static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KiB per-CTA shared memory limit");
@@ -805,19 +799,6 @@ __device__ void run_epilogue(const QkvParams& p, const Sched& sc, uint8_t* smem,
     __syncwarp();
 }
 
-// Split-mode partial rows are parked with each head's 128 columns permuted so
-// that lane q of an octet finds its sixteen columns (32c + 8k + q) together:
-// column 32c + 8k + q of head slot hs sits at float hs*128 + 16q + 4c + k.
-// `cc` is the TMEM chunk (32 columns) that `v` holds.
-__device__ __forceinline__ void park_chunk_permuted(float* row, int cc, const uint32_t (&v)[32]) {
-    const int base = (cc >> 2) * 128 + (cc & 3) * 4;
-#pragma unroll
-    for (int q = 0; q < 8; ++q)
-        *reinterpret_cast<float4*>(row + base + 16 * q) =
-            make_float4(__uint_as_float(v[q]), __uint_as_float(v[8 + q]),
-                        __uint_as_float(v[16 + q]), __uint_as_float(v[24 + q]));
-}
-
 // Split mode, step 1 (epilogue warps): park this CTA's FP32 partial
 // accumulator of the tile in its own shared memory (the operand ring, idle by
 // now), rows of PART_STRIDE bytes.  Only warps holding valid rows copy.
@@ -880,7 +861,12 @@ __device__ void run_split_partial(const QkvParams& p, const Sched& sc, uint8_t* 
             uint32_t v[32];
             tmem_ld_32cols(tmem_base + lane_addr + c * 32, v);
             tmem_ld_wait();
-            if (r < p.L) park_chunk_permuted(slot, c, v);
+            if (r < p.L)
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    reinterpret_cast<float4*>(slot + c * 32)[i] =
+                        make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                    __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
         }
         fence_proxy_async_smem();          // read next by a bulk copy (async proxy)
         return;
@@ -891,42 +877,57 @@ __device__ void run_split_partial(const QkvParams& p, const Sched& sc, uint8_t* 
         uint32_t r[32];
         tmem_ld_32cols(tmem_base + lane_addr + c * 32, r);
         tmem_ld_wait();
-        park_chunk_permuted(row, c, r);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            reinterpret_cast<float4*>(row + c * 32)[i] =
+                make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                            __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
     }
 }
 
-// Split mode, the last step for one item (token row m, head h) on an octet of
-// eight lanes.  Lane q of the octet owns columns 32c + 8k + q (c, k = 0..3);
-// acc[c] holds columns 32c + q + 8k in .x .. .w (k = 0..3), cs/sn the cos|sin
-// of columns j = 32c + 8k + q < 64 at index 4c + k.  With this ownership
-// torch's CPU summation order for the sum of squares is local to a lane
-// (accumulator k of lane q sums columns 32c + 8k + q over c = 0..3, the
-// accumulators are added k = 0..3) followed by the eight lanes left to
-// right, and the NeoX partner of column j (j + 64: c + 2) is in the same
-// lane.  The row leaves through the octet's staging row: each lane writes its
-// sixteen BF16 values, then stores 32 contiguous bytes into the destination
-// rank's receive buffer.  Every lane of the warp calls this together (the
-// shuffles and warp barriers); an octet with `valid` false stores nothing.
-__device__ __forceinline__ void split_octet_emit(const QkvParams& p, const float4 (&acc)[4],
-                                                 int m, int h, bool valid, const float* gam,
-                                                 const float (&cs)[8], const float (&sn)[8],
-                                                 __nv_bfloat16* stage, int q) {
+// Split mode, step 2 (every warp of every cluster CTA, after a cluster
+// barrier): one item = one valid token row x one head.  A warp takes two items
+// at a time; lane l owns columns 4l..4l+3 of the head, loads the partials of
+// every cluster CTA at once (coalesced distributed-shared-memory reads) and
+// sums them in rank order (deterministic).  The RMSNorm sum is a warp
+// reduction, the NeoX partner of lane l is lane l^16, and the row leaves as
+// one coalesced 256-byte store into the destination rank's receive buffer.
+// cos|sin of columns 4l..4l+3 (mod 64) at token row m's position, for a Q/K
+// head (V heads are not rotated); issued before the partial sums are read so
+// the two latencies overlap.
+struct SplitRope {
+    float4 cs, sn;
+};
+
+__device__ __forceinline__ SplitRope split_item_rope(const QkvParams& p, const int32_t* rope_rows,
+                                                    int row, int h, int lane) {
+    SplitRope r;
+    r.cs = r.sn = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (h < p.q_heads + p.kv_heads) {
+        const float* base = p.rope + static_cast<int64_t>(rope_rows[row]) * 128 + 4 * (lane & 15);
+        r.cs = __ldg(reinterpret_cast<const float4*>(base));
+        r.sn = __ldg(reinterpret_cast<const float4*>(base + 64));
+    }
+    return r;
+}
+
+__device__ __forceinline__ void split_item_emit(const QkvParams& p, const float4& acc, int m,
+                                                int h, const float* gam, int lane,
+                                                const SplitRope& rope) {
+    // BF16 projection of columns 4l..4l+3 of head h, token row m.
+    const uint32_t u0 = pack_bf16x2(acc.x, acc.y);
+    const uint32_t u1 = pack_bf16x2(acc.z, acc.w);
     const bool r16 = !p.fp32_epilogue;
-    float u[4][4];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        u[c][0] = round_if(acc[c].x, r16);
-        u[c][1] = round_if(acc[c].y, r16);
-        u[c][2] = round_if(acc[c].z, r16);
-        u[c][3] = round_if(acc[c].w, r16);
+    float v[4];
+    if (r16) {
+        const float2 a = unpack_bf16x2(u0), b = unpack_bf16x2(u1);
+        v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    } else {
+        v[0] = acc.x; v[1] = acc.y; v[2] = acc.z; v[3] = acc.w;
     }
-    if (valid && p.gemm_out != nullptr) {
-        __nv_bfloat16* d = p.gemm_out + static_cast<int64_t>(m) * p.N + h * 128;
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int k = 0; k < 4; ++k) d[32 * c + 8 * k + q] = __float2bfloat16_rn(u[c][k]);
-    }
+    if (p.gemm_out != nullptr)
+        *reinterpret_cast<uint2*>(p.gemm_out + static_cast<int64_t>(m) * p.N + h * 128 + 4 * lane) =
+            make_uint2(u0, u1);
     int comp, head_id, per_gpu;
     if (h < p.q_heads) {
         comp = 0; head_id = h; per_gpu = p.q_per_gpu;
@@ -935,75 +936,66 @@ __device__ __forceinline__ void split_octet_emit(const QkvParams& p, const float
     } else {
         comp = 2; head_id = h - p.q_heads - p.kv_heads; per_gpu = p.kv_per_gpu;
     }
-    float o[4][4];
+    const int dst = head_id / per_gpu;
+    const int dst_col = head_id % per_gpu;
+    uint2 out = make_uint2(u0, u1);
     if (comp < 2) {
-        float lane_sum = 0.f;
+        // The sum of squares in the order of torch's CPU reduction (as in
+        // emit_head): column j = 4 lane + e belongs to accumulator k =
+        // (lane / 2) % 4, eight-lane slot 4 (lane % 2) + e, step lane / 8.
+        // Every shuffle reads values that no earlier step of this sum changed.
+        float sq[4], acc[4], a[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            float a = __fmul_rn(u[0][k], u[0][k]);
+        for (int e = 0; e < 4; ++e) acc[e] = sq[e] = __fmul_rn(v[e], v[e]);
 #pragma unroll
-            for (int c = 1; c < 4; ++c) a = __fadd_rn(a, __fmul_rn(u[c][k], u[c][k]));
-            lane_sum = k == 0 ? a : __fadd_rn(lane_sum, a);
+        for (int step = 8; step <= 24; step += 8) {        // steps 1..3 into lanes 0..7
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                acc[e] = __fadd_rn(acc[e], __shfl_down_sync(0xffffffffu, sq[e], step));
         }
-        float ss = __shfl_sync(0xffffffffu, lane_sum, 0, 8);
 #pragma unroll
-        for (int l = 1; l < 8; ++l) ss = __fadd_rn(ss, __shfl_sync(0xffffffffu, lane_sum, l, 8));
-        const float scale = norm_scale(ss, comp == 0 ? p.q_eps : p.k_eps);
-        const float* g = gam + comp * 128;
-        float n[4][4];
+        for (int e = 0; e < 4; ++e) a[e] = acc[e];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int k = 2; k <= 6; k += 2) {                  // accumulators 1..3 into lanes 0, 1
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-                n[c][k] = round_if(__fmul_rn(__fmul_rn(u[c][k], scale), g[32 * c + 8 * k + q]),
-                                   r16);
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float cj = cs[4 * c + k], sj = sn[4 * c + k];
-                o[c][k] = __fsub_rn(__fmul_rn(n[c][k], cj), __fmul_rn(n[c + 2][k], sj));
-                o[c + 2][k] = __fadd_rn(__fmul_rn(n[c + 2][k], cj), __fmul_rn(n[c][k], sj));
-            }
-    } else {
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int k = 0; k < 4; ++k) o[c][k] = u[c][k];
-    }
-#pragma unroll
-    for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int k = 0; k < 4; ++k) stage[32 * c + 8 * k + q] = __float2bfloat16_rn(o[c][k]);
-    __syncwarp();
-    if (valid) {
-        const int dst = head_id / per_gpu;
-        const int dst_col = head_id % per_gpu;
-        const int64_t cols = static_cast<int64_t>(per_gpu) * 128;
-        __nv_bfloat16* base = static_cast<__nv_bfloat16*>(p.out_base[comp * FU_MAX_SP + dst]);
-        uint4* d = reinterpret_cast<uint4*>(
-            base + (static_cast<int64_t>(p.sp_rank) * p.L + m) * cols + dst_col * 128 + 16 * q);
-        const uint4* src = reinterpret_cast<const uint4*>(stage + 16 * q);
-        d[0] = src[0];
-        d[1] = src[1];
-    }
-    __syncwarp();                           // the staging row is free again
-}
-
-// cos|sin of the eight columns j = 32c + 8k + q < 64 that octet lane q rotates
-// (zero for a V head, which is not rotated); `row` is the table row (global
-// or shared memory).
-__device__ __forceinline__ void octet_rope(const QkvParams& p, const float* row, int h, int q,
-                                           float (&cs)[8], float (&sn)[8]) {
-    const bool rotated = h < p.q_heads + p.kv_heads;
-#pragma unroll
-    for (int c = 0; c < 2; ++c)
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int j = 32 * c + 8 * k + q;
-            cs[4 * c + k] = rotated ? row[j] : 0.f;
-            sn[4 * c + k] = rotated ? row[64 + j] : 0.f;
+            for (int e = 0; e < 4; ++e)
+                a[e] = __fadd_rn(a[e], __shfl_down_sync(0xffffffffu, acc[e], k));
         }
+        float hi[4];                                         // slots 4..7 (lane 1) to lane 0
+#pragma unroll
+        for (int e = 0; e < 4; ++e) hi[e] = __shfl_down_sync(0xffffffffu, a[e], 1);
+        float ss = a[0];
+#pragma unroll
+        for (int e = 1; e < 4; ++e) ss = __fadd_rn(ss, a[e]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ss = __fadd_rn(ss, hi[e]);
+        ss = __shfl_sync(0xffffffffu, ss, 0);
+        const float eps = comp == 0 ? p.q_eps : p.k_eps;
+        const float scale = norm_scale(ss, eps);
+        const float* g = gam + comp * 128 + 4 * lane;
+        float n[4], partner[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) n[i] = round_if(__fmul_rn(__fmul_rn(v[i], scale), g[i]), r16);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, n[i], 16);
+        const float c4[4] = {rope.cs.x, rope.cs.y, rope.cs.z, rope.cs.w};
+        const float s4[4] = {rope.sn.x, rope.sn.y, rope.sn.z, rope.sn.w};
+        float r[4];
+        if (lane < 16) {        // lo half: lo*cos - hi*sin
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                r[i] = __fsub_rn(__fmul_rn(n[i], c4[i]), __fmul_rn(partner[i], s4[i]));
+        } else {                // hi half: hi*cos + lo*sin
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                r[i] = __fadd_rn(__fmul_rn(n[i], c4[i]), __fmul_rn(partner[i], s4[i]));
+        }
+        out = make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
+    }
+    const int64_t cols = static_cast<int64_t>(per_gpu) * 128;
+    __nv_bfloat16* base = static_cast<__nv_bfloat16*>(p.out_base[comp * FU_MAX_SP + dst]);
+    *reinterpret_cast<uint2*>(base + (static_cast<int64_t>(p.sp_rank) * p.L + m) * cols +
+                              dst_col * 128 + 4 * lane) = out;
 }
 
 __device__ void run_split_reduce(const QkvParams& p, const Sched& sc, uint8_t* smem,
@@ -1032,70 +1024,77 @@ __device__ void run_split_reduce(const QkvParams& p, const Sched& sc, uint8_t* s
     const int rows = min(BM, p.L - m_blk * BM);
     const int heads_here = min(2, p.heads - n_blk * 2);
     const int items = rows * heads_here;
-    // One item per octet of lanes; every octet of every warp of every cluster
-    // CTA takes items (the producer and MMA warps are idle by now).  Octet o
-    // of warp w on cluster rank r takes items (4w + o) * splits + r + j *
-    // workers.  Each step sums the partials requested by the previous step
-    // (rank order: deterministic), requests the next step's partials over
-    // distributed shared memory and its RoPE values, then normalises, rotates
-    // and stores the current item, so the remote reads of one step overlap the
-    // arithmetic of the step before.
-    const int octet = lane >> 3, q = lane & 7;
-    const int workers = NUM_THREADS / 32 * 4 * p.splits;
+    // Every warp of every cluster CTA takes items: the producer and MMA warps
+    // are idle by now, and each item's chain of shuffles and roundings is
+    // latency-bound, so more warps in flight shorten the reduction.
+    const int workers = NUM_THREADS / 32 * p.splits;
     const uint32_t part = smem_u32(smem + OFF_A);
     const int32_t* rope_rows = reinterpret_cast<const int32_t*>(smem + OFF_STG);
-    __nv_bfloat16* stage =
-        reinterpret_cast<__nv_bfloat16*>(smem + OFF_OCT + (warp * 4 + octet) * OCT_STAGE_BYTES);
+    // Item i: row i / heads_here, head slot i % heads_here.  A warp takes two
+    // items per step (i0 and i0 + workers).  Each step first sums the partials
+    // requested by the previous step (in rank order: deterministic), then
+    // requests the next step's partials over distributed shared memory and its
+    // RoPE values, and only then normalises, rotates and stores the current
+    // items, so the remote reads of one step overlap the arithmetic of the
+    // step before.
     struct Raw {
-        float4 v[4][FU_MAX_SP];
-        float cs[8], sn[8];
+        float4 v[2][FU_MAX_SP];
+        SplitRope rope[2];
     };
-    auto request = [&](int i, Raw& raw) {
-        i = min(i, items - 1);
-        const int r = i / heads_here, hs = i % heads_here;
-        octet_rope(p, p.rope + static_cast<int64_t>(rope_rows[r]) * 128, n_blk * 2 + hs, q,
-                   raw.cs, raw.sn);
-        const uint32_t local = part + r * PART_STRIDE + (hs * 128 + 16 * q) * 4;
+    auto request = [&](int i0, Raw& raw) {
 #pragma unroll
-        for (int k = 0; k < FU_MAX_SP; ++k)
-            if (k < p.splits)
+        for (int k = 0; k < 2; ++k) {
+            const int i = min(i0 + k * workers, items - 1);
+            raw.rope[k] = split_item_rope(p, rope_rows, i / heads_here,
+                                          n_blk * 2 + i % heads_here, lane);
+        }
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    raw.v[c][k] = ld_cluster_f32x4(map_cluster_smem(local + 16 * c, k));
+        for (int k = 0; k < 2; ++k) {
+            const int i = min(i0 + k * workers, items - 1);
+            const uint32_t local = part + (i / heads_here) * PART_STRIDE +
+                                   ((i % heads_here) * 128 + 4 * lane) * 4;
+#pragma unroll
+            for (int r = 0; r < FU_MAX_SP; ++r)
+                if (r < p.splits) raw.v[k][r] = ld_cluster_f32x4(map_cluster_smem(local, r));
+        }
     };
-    const int warp_first = warp * 4 * p.splits + sc.split;      // octet 0's first item
-    int i = (warp * 4 + octet) * p.splits + sc.split;
+    const int first = warp * p.splits + sc.split;
     Raw raw;
-    if (warp_first < items) request(i, raw);
-    for (int wi = warp_first; wi < items; wi += workers, i += workers) {
-        float4 acc[4];
-        float cs[8], sn[8];
+    if (first < items) request(first, raw);
+    for (int i0 = first; i0 < items; i0 += 2 * workers) {
+        float4 acc[2];
+        SplitRope rope[2];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            acc[c] = raw.v[c][0];
+        for (int k = 0; k < 2; ++k) {
+            acc[k] = raw.v[k][0];
 #pragma unroll
-            for (int k = 1; k < FU_MAX_SP; ++k)
-                if (k < p.splits) {
-                    acc[c].x += raw.v[c][k].x; acc[c].y += raw.v[c][k].y;
-                    acc[c].z += raw.v[c][k].z; acc[c].w += raw.v[c][k].w;
+            for (int r = 1; r < FU_MAX_SP; ++r)
+                if (r < p.splits) {
+                    acc[k].x += raw.v[k][r].x; acc[k].y += raw.v[k][r].y;
+                    acc[k].z += raw.v[k][r].z; acc[k].w += raw.v[k][r].w;
                 }
+            rope[k] = raw.rope[k];
         }
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            cs[t] = raw.cs[t];
-            sn[t] = raw.sn[t];
+        if (i0 + 2 * workers < items) request(i0 + 2 * workers, raw);
+        // One copy of the item code, looped: the step's code then stays in the
+        // instruction cache (two inlined copies made the warps wait on
+        // instruction fetch for most of each step).
+#pragma unroll 1
+        for (int k = 0; k < 2; ++k) {
+            const int i = i0 + k * workers;
+            if (i < items)
+                split_item_emit(p, acc[0], m_blk * BM + i / heads_here,
+                                n_blk * 2 + i % heads_here, gam, lane, rope[0]);
+            acc[0] = acc[1];                    // the second item moves up
+            rope[0] = rope[1];
         }
-        if (wi + workers < items) request(i + workers, raw);
-        const int ic = min(i, items - 1);
-        split_octet_emit(p, acc, m_blk * BM + ic / heads_here, n_blk * 2 + ic % heads_here,
-                         i < items, gam, cs, sn, stage, q);
     }
 }
 
 // Split push mode, the leader's epilogue warps: every rank's rows of the
-// single row block are in this CTA's shared memory, [rank][row][256 cols]
-// (columns permuted as parked).  One item = one valid token row x one head on
-// an octet of lanes; partials summed in rank order (deterministic), then the
+// single row block are in this CTA's shared memory, [rank][row][256 cols].
+// One item = one valid token row x one head, one warp per item, lane l owning
+// columns 4l..4l+3; partials summed in rank order (deterministic), then the
 // same normalisation, rotation and store as the distributed reduction.
 __device__ void run_split_push_reduce(const QkvParams& p, const Sched& sc, uint8_t* smem,
                                       const float* gam, volatile int* abort_flag,
@@ -1110,29 +1109,23 @@ __device__ void run_split_push_reduce(const QkvParams& p, const Sched& sc, uint8
     const int items = rows * heads_here;
     const float* rope_smem = reinterpret_cast<const float*>(smem + push_rope_offset(p));
     const float* slots = reinterpret_cast<const float*>(smem + OFF_PUSH);
-    // One item per octet of lanes of the four epilogue warps.
-    const int octet = lane >> 3, q = lane & 7;
-    __nv_bfloat16* stage =
-        reinterpret_cast<__nv_bfloat16*>(smem + OFF_OCT + (warp * 4 + octet) * OCT_STAGE_BYTES);
-    for (int wi = (warp - 2) * 4; wi < items; wi += NUM_EPI_THREADS / 8) {
-        const int i = wi + octet;
-        const int ic = min(i, items - 1);
-        const int r = ic / heads_here, hs = ic % heads_here;
+    for (int i = warp - 2; i < items; i += NUM_EPI_THREADS / 32) {
+        const int r = i / heads_here, hs = i % heads_here;
         const int h = tile.n_blk * 2 + hs;
-        float cs[8], sn[8];
-        octet_rope(p, rope_smem + r * 128, h, q, cs, sn);
-        float4 acc[4];
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-            acc[c] = *reinterpret_cast<const float4*>(slots + r * BN + hs * 128 + 16 * q + 4 * c);
-        for (int k = 1; k < p.splits; ++k)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const float4 v = *reinterpret_cast<const float4*>(
-                    slots + (k * rows + r) * BN + hs * 128 + 16 * q + 4 * c);
-                acc[c].x += v.x; acc[c].y += v.y; acc[c].z += v.z; acc[c].w += v.w;
-            }
-        split_octet_emit(p, acc, r, h, i < items, gam, cs, sn, stage, q);
+        SplitRope rope;
+        rope.cs = rope.sn = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (h < p.q_heads + p.kv_heads) {
+            const float* cs = rope_smem + r * 128 + 4 * (lane & 15);
+            rope.cs = *reinterpret_cast<const float4*>(cs);
+            rope.sn = *reinterpret_cast<const float4*>(cs + 64);
+        }
+        float4 acc = reinterpret_cast<const float4*>(slots + r * BN + hs * 128)[lane];
+        for (int k = 1; k < p.splits; ++k) {
+            const float4 v =
+                reinterpret_cast<const float4*>(slots + (k * rows + r) * BN + hs * 128)[lane];
+            acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+        }
+        split_item_emit(p, acc, r, h, gam, lane, rope);
     }
 }
 
