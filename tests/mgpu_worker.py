@@ -15,7 +15,8 @@ checks this rank's outputs three ways (the criteria of the one-GPU tests):
 
 Placement, padding and untouched capacity are checked bit for bit on exact
 inputs.  Then back-to-back calls and CUDA-graph replays without a host
-rendezvous (bit-identical to a checked call), the output side, and finally a
+rendezvous (bit-identical to a checked call; at L=1 also with static
+weights), the output side, and finally a
 host-side fault: one rank skips a call and its peers' bounded wait must
 report it.
 """
@@ -110,11 +111,12 @@ def run_case(cfg, tokens_list, gloo):
                                 sp_size=cfg.sp_size, seed=seed)
         return x, p, params, None
 
-    def call(x, p, gp, proj=None, check=True):
+    def call(x, p, gp, proj=None, check=True, static_weights=False):
         return ctx.ulysses_qkv_forward(x, gp["qkv_weight"], p, gp["q_norm_weight"],
                                        gp["k_norm_weight"], gp["rope_cache"],
                                        q_epsilon=gp["q_epsilon"], k_epsilon=gp["k_epsilon"],
-                                       check=check, _projection_out=proj)
+                                       check=check, static_weights=static_weights,
+                                       _projection_out=proj)
 
     try:
         for tokens in tokens_list:
@@ -190,6 +192,20 @@ def run_case(cfg, tokens_list, gloo):
         for g, f, name in zip(got, first, "QKV"):
             if not bits_equal(g, f):
                 failures.append(f"{cfg.name} back-to-back {name}: differs from the checked call")
+        # The same calls with static weights (the first weight stages read
+        # before the dependency wait), at the decode size the flag serves.
+        x1_c, p1_c, params1_c, _ = inputs(1, seed=98)
+        g1 = {k: (v.to(dev) if torch.is_tensor(v) else v) for k, v in params1_c.items()}
+        x1, p1 = x1_c.to(dev), p1_c.to(dev)
+        dist.barrier(group=gloo)
+        plain = [g.clone() for g in call(x1, p1, g1)]
+        dist.barrier(group=gloo)
+        for _ in range(20):
+            got = call(x1, p1, g1, check=False, static_weights=True)
+        ctx.check()
+        for g, f, name in zip(got, plain, "QKV"):
+            if not bits_equal(g, f):
+                failures.append(f"{cfg.name} static weights {name}: differs from the plain call")
     finally:
         torch.cuda.synchronize()
         dist.barrier(group=gloo)
